@@ -1,0 +1,448 @@
+"""Benchmark: Cl(6,0) full-cycle training at batch 2^22 per GPU, float64.
+
+One step = one pass of the fused full cycle over the GPU's minibatch:
+forward x*W -> residual -> 0.5|r|^2 -> parameter VJP -> (NCCL all-gather of the
+per-rank gradient record when N > 1) -> Adam (lr 1e-3, betas 0.9/0.999,
+eps 1e-8, V8 semantics). Data is synthetic: X ~ U[-1,1], targets
+Y = W* X-products + N(0, 1e-3) noise with W* ~ N(0, 1), W0 ~ N(0, std 1/8).
+X and T are 2 GiB each per GPU, far larger than the 126 MB L2, so no flush is
+needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+For N > 1 launch one process per GPU with torch.distributed.run; rank 0 prints
+one JSON line. `value` is device-timed (CUDA events, max over ranks);
+`e2e` runs the same step through the public host-buffer call
+(geo_b200_trainer_step_host) from pinned host memory, timed on the host around
+that synchronous call (max over ranks). `--impl reference` times the
+reference's own CPU code (oracle/_ref, compiled from its sources) on the host
+cores for the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+METRIC = "multivector products/s and training samples/s at Cl(6,0), % of HBM/FP64 roofline"
+UNIT = "training samples/s"
+BYTES_PER_SAMPLE = 2 * 64 * 8     # read x and t once per step (float64, 64 blades)
+FLOPS_PER_SAMPLE = 4 * 64 * 64    # forward 2*4^n + parameter VJP 2*4^n
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--batch-log2", type=int, default=22, help="per-GPU batch = 2^k (22 is the headline shape)")
+    p.add_argument("--negative", type=int, default=0, help="q of Cl(6-q, q); 0 = Cl(6,0)")
+    p.add_argument("--no-extras", action="store_true", help="skip e2e, Cl(3,3) and cpu_baseline legs")
+    return p.parse_args()
+
+
+# --------------------------------------------------------------------------- helpers
+def dist_setup(n_gpus):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-i", str(index), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.3)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, f[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peaks():
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, STREAM-style copy)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6.65 TB/s (profiling recipe)"
+
+
+# --------------------------------------------------------------------------- data
+def make_data(lib, sig, batch, seed, left=0):
+    """X ~ U[-1,1]; T = x*W* (+ noise 1e-3) via the library's own forward kernel."""
+    import torch
+
+    from geometricelementaryoperators_b200 import abi
+
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    X = torch.rand((batch, 64), dtype=torch.float64, device="cuda", generator=gen).mul_(2).sub_(1)
+    w_star = torch.randn(64, dtype=torch.float64, device="cuda", generator=gen)
+    T = torch.empty_like(X)
+    plan = abi.BatchGpPlan()
+    assert lib.geo_batch_gp_plan_init(ctypes.byref(plan), 6, abi.sig_array(sig)) == 0
+    cplan = abi.CudaPlan()
+    assert lib.geo_batch_gp_cuda_plan_upload(ctypes.byref(cplan), ctypes.byref(plan)) == 0
+    st = lib.geo_batch_gp_cuda_planned_forward_f64(ctypes.byref(cplan), ctypes.c_void_p(X.data_ptr()), batch,
+                                                   ctypes.c_void_p(w_star.data_ptr()), left,
+                                                   ctypes.c_void_p(T.data_ptr()),
+                                                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == 0
+    torch.cuda.synchronize()
+    lib.geo_batch_gp_cuda_plan_destroy(ctypes.byref(cplan))
+    T.add_(torch.randn(T.shape, dtype=torch.float64, device="cuda", generator=gen), alpha=1e-3)
+    w0 = torch.randn(64, dtype=torch.float64, generator=torch.Generator().manual_seed(seed + 1)) * 0.125
+    return X, T, w0.numpy()
+
+
+class Trainer:
+    def __init__(self, lib, sig, w0, left=0):
+        from geometricelementaryoperators_b200 import abi
+
+        self.lib = lib
+        self.h = ctypes.c_void_p()
+        cfg = abi.OptimizerConfig(2, 1e-3, 0.9, 0.999, 1e-8)
+        import numpy as np
+
+        self.w0 = np.ascontiguousarray(w0, dtype=np.float64)
+        st = lib.geo_b200_trainer_create(ctypes.byref(self.h), 6, abi.sig_array(sig), left,
+                                         self.w0.ctypes.data_as(ctypes.c_void_p), ctypes.byref(cfg))
+        if st != 0:
+            raise RuntimeError(f"trainer_create failed: {st}")
+
+    def destroy(self):
+        self.lib.geo_b200_trainer_destroy(self.h)
+
+
+# --------------------------------------------------------------------------- reference arm
+def _reference_worker(args):
+    """Run the reference CPU path (compiled from its sources) on `chunks` chunks of
+    1024 samples: batch_gp forward -> residual -> batch_gp VJP, the reference's
+    fastest regime. Returns samples processed."""
+    chunks, seed, signature = args
+    import numpy as np
+
+    from oracle.oracle import Reference
+
+    ref = Reference()
+    rng = np.random.default_rng(seed)
+    x = rng.uniform(-1, 1, (1024, 64))
+    t = rng.uniform(-1, 1, (1024, 64))
+    w = rng.normal(0, 0.125, 64)
+    done = 0
+    for _ in range(chunks):
+        st, y = ref.forward(signature, x, w, False)
+        r = y - t
+        st2, g = ref.vjp(signature, x, r, False)
+        assert st == 0 and st2 == 0
+        done += x.shape[0]
+    return done
+
+
+def reference_step(pool, workers, chunks, signature):
+    t0 = time.perf_counter()
+    done = sum(pool.map(_reference_worker, [(chunks, 17 + i, signature) for i in range(workers)]))
+    return done, time.perf_counter() - t0
+
+
+def run_reference_arm(args, world, rank):
+    """The reference's own CPU implementation on all host threads (rank 0 only)."""
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+
+    sig = [1] * (6 - args.negative) + [-1] * args.negative
+    if not orc.REF_SO.exists():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libgeo_ref.so was not built "
+                          "(the reference sources were not present at build time)"}))
+        return
+    import multiprocessing as mp
+
+    workers = os.cpu_count() or 1
+    ctx = mp.get_context("spawn")
+    chunks = 2
+    with ctx.Pool(workers) as pool:
+        reference_step(pool, workers, 1, sig)  # import + warm
+        # size chunks so one step is ~1 s of work on every core
+        done, dt = reference_step(pool, workers, chunks, sig)
+        chunks = max(1, int(chunks * 1.0 / max(dt, 1e-3)))
+        for _ in range(args.warmup):
+            reference_step(pool, workers, chunks, sig)
+        total, elapsed = 0, 0.0
+        for _ in range(args.steps):
+            done, dt = reference_step(pool, workers, chunks, sig)
+            total += done
+            elapsed += dt
+    value = total / elapsed
+    sample = f"{workers} processes x {chunks} chunks of 1024 samples per step (forward+VJP; Adam is O(64))"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * elapsed / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"Cl({6 - args.negative},{args.negative}) full-cycle training step, float64, "
+                               "reference CPU batch_gp forward+VJP on 1024-sample chunks", "blades": 64},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": workers, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_leg(negative: int) -> dict:
+    """Reference CPU code, 1 core, bounded sample of ~10 s on the 2^22 workload's shape."""
+    from oracle import oracle as orc
+
+    sig = [1] * (6 - negative) + [-1] * negative
+    if orc.REF_SO.exists():
+        kind = "reference"
+        worker = _reference_worker
+    else:
+        return {"value": None, "unit": UNIT, "cores": 1, "kind": "reference",
+                "sample": "unavailable: oracle/_ref not built"}
+    done, t0, chunks = 0, time.perf_counter(), 0
+    while time.perf_counter() - t0 < 10.0 or chunks < 8:
+        done += worker((1, 99 + chunks, sig))
+        chunks += 1
+    dt = time.perf_counter() - t0
+    return {"value": done / dt, "unit": UNIT, "cores": 1, "kind": kind,
+            "sample": f"{chunks} chunks of 1024 samples of the Cl(6,{negative}) shape (forward+VJP), {dt:.1f} s"}
+
+
+# --------------------------------------------------------------------------- main arm
+def run_b200(args, world, rank, local):
+    import numpy as np
+    import torch
+
+    from geometricelementaryoperators_b200 import abi
+
+    lib = abi.lib()
+    batch = 1 << args.batch_log2
+    q = args.negative
+    sig = [1] * (6 - q) + [-1] * q
+    X, T, w0 = make_data(lib, sig, batch, 1234 + rank)
+    tr = Trainer(lib, sig, w0)
+    comm = ctypes.c_void_p()
+    if world > 1:
+        import torch.distributed as dist
+
+        uid = (ctypes.c_ubyte * 128)()
+        if rank == 0:
+            assert lib.geo_b200_comm_unique_id(uid) == 0
+        obj = [bytes(uid)]
+        dist.broadcast_object_list(obj, src=0)
+        uid = (ctypes.c_ubyte * 128).from_buffer_copy(obj[0])
+        st = lib.geo_b200_comm_create(ctypes.byref(comm), rank, world, uid, 120000)
+        if st != 0:
+            raise RuntimeError(f"comm_create failed: {st}")
+        assert lib.geo_b200_trainer_attach_comm(tr.h, comm) == 0
+    stream = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    xp, tp = ctypes.c_void_p(X.data_ptr()), ctypes.c_void_p(T.data_ptr())
+    scale = 1.0 / (batch * world)
+
+    def step():
+        st = lib.geo_b200_trainer_accumulate_device(tr.h, xp, tp, batch, sp)
+        if st != 0:
+            raise RuntimeError(f"accumulate failed: {st}")
+        st = lib.geo_b200_trainer_apply(tr.h, scale, sp)
+        if st != 0:
+            raise RuntimeError(f"apply failed: {st}")
+
+    for _ in range(args.warmup):
+        step()
+    loss0 = ctypes.c_double()
+    assert lib.geo_b200_trainer_sync(tr.h, ctypes.byref(loss0)) == 0
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = ClockSampler(torch.cuda.current_device() if world == 1 else local)
+    time.sleep(0.4)
+    k_start = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    k_end = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for i in range(args.steps):
+        k_start[i].record(stream)
+        st = lib.geo_b200_trainer_accumulate_device(tr.h, xp, tp, batch, sp)
+        k_end[i].record(stream)
+        st |= lib.geo_b200_trainer_apply(tr.h, scale, sp)
+        if st != 0:
+            raise RuntimeError(f"step failed: {st}")
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clock_info = clocks.stop()
+    loss = ctypes.c_double()
+    status = lib.geo_b200_trainer_sync(tr.h, ctypes.byref(loss))
+    if status != 0:
+        raise RuntimeError(f"training reported status {status}")
+    step_ms = max_over_ranks(start.elapsed_time(end) / args.steps, world)
+    kernel_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in zip(k_start, k_end)) / args.steps, world)
+    value = batch * world / (step_ms / 1e3)
+
+    extras = {}
+    if not args.no_extras:
+        # Same step on Cl(3,3) (the second signature of the headline config).
+        X2, T2, w2 = X, T, w0
+        tr33 = Trainer(lib, [1, 1, 1, -1, -1, -1], w2)
+        if world > 1:
+            assert lib.geo_b200_trainer_attach_comm(tr33.h, comm) == 0
+        for _ in range(args.warmup):
+            assert lib.geo_b200_trainer_step_device(tr33.h, xp, tp, batch, scale, sp) == 0
+        torch.cuda.synchronize()
+        barrier(world)
+        s33, e33 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s33.record(stream)
+        for _ in range(args.steps):
+            assert lib.geo_b200_trainer_step_device(tr33.h, xp, tp, batch, scale, sp) == 0
+        e33.record(stream)
+        torch.cuda.synchronize()
+        assert lib.geo_b200_trainer_sync(tr33.h, None) == 0
+        ms33 = max_over_ranks(s33.elapsed_time(e33) / args.steps, world)
+        extras["cl33"] = {"value": batch * world / (ms33 / 1e3), "ms_per_step": ms33}
+        tr33.destroy()
+
+        # End to end through the public host-buffer call from pinned memory.
+        hx = X.cpu().pin_memory()
+        ht = T.cpu().pin_memory()
+        e2e_steps = max(3, min(args.steps, 10))
+        loss_h = ctypes.c_double()
+        hxp, htp = ctypes.c_void_p(hx.data_ptr()), ctypes.c_void_p(ht.data_ptr())
+        assert lib.geo_b200_trainer_step_host(tr.h, hxp, htp, batch, scale, ctypes.byref(loss_h)) == 0
+        torch.cuda.synchronize()
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            assert lib.geo_b200_trainer_step_host(tr.h, hxp, htp, batch, scale, ctypes.byref(loss_h)) == 0
+        torch.cuda.synchronize()
+        e2e_s = max_over_ranks((time.perf_counter() - t0) / e2e_steps, world)
+        extras["e2e"] = {"value": batch * world / e2e_s, "unit": UNIT,
+                         "h2d_bytes_per_step": 2 * batch * 64 * 8 * world, "d2h_bytes_per_step": 8 * world,
+                         "timing": "host wall clock around the synchronous host-buffer call, max over ranks",
+                         "steps": e2e_steps}
+        del hx, ht
+
+    hbm_peak, peak_src = peaks()
+    algo_bytes = batch * BYTES_PER_SAMPLE
+    achieved = algo_bytes / (kernel_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak, "traffic": None, "peak_source": peak_src,
+                "kernel": "tiled_kernel<64, cycle> (+ record reduction) per step, CUDA events on the launch stream",
+                "kernel_ms": kernel_ms,
+                "fp64_flops_achieved_tflops": batch * FLOPS_PER_SAMPLE / (kernel_ms / 1e3) / 1e12}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": f"Cl({6 - q},{q}) full-cycle training step (forward + parameter VJP + MSE + "
+                                   "Adam), parameter on the right, float64, batch 2^%d per GPU" % args.batch_log2,
+                       "batch_per_gpu": batch, "global_batch": batch * world, "blades": 64,
+                       "signature": sig, "optimizer": "adam lr=1e-3 b=(0.9,0.999) eps=1e-8",
+                       "l2": "inputs 4 GiB per GPU per step > 126 MB L2; no flush needed",
+                       "parallelism": f"dp{world}"},
+            "roofline": roofline,
+            "gpu_launches": args.steps * 3,
+            "clocks": clock_info,
+            "final_loss_sum": loss.value,
+        }
+        if "e2e" in extras:
+            line["e2e"] = extras["e2e"]
+        if "cl33" in extras:
+            line["cl33"] = extras["cl33"]
+        if world == 1 and not args.no_extras:
+            line["cpu_baseline"] = cpu_baseline_leg(q)
+        print(json.dumps(line), flush=True)
+    tr.destroy()
+    if world > 1:
+        lib.geo_b200_comm_destroy(comm)
+
+
+def main():
+    args = parse()
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference_arm(args, world, rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        run_b200(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,127 @@
+// geo_internal.h -- internal declarations shared by the sm_100a kernels and the
+// C-ABI translation units of libgeo_b200.so. Nothing here is exported.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "geo/batch_gp.h"
+#include "geo/operator_kernel.h"
+
+namespace geo {
+
+constexpr int kMaxDim = 6;
+constexpr int kMaxBlades = 64;
+
+// Baked routing/sign plan for one (dimension, signature, side) triple.
+// neg[i] bit p is set when sigma(i, p) = -1, where sigma is the sign of the
+// term that pairs input blade i with parameter blade p:
+//   parameter on the right: sigma(i, p) = s(i, p)  (term left=i, right=p)
+//   parameter on the left:  sigma(i, p) = s(p, i)  (term left=p, right=i)
+// and the output blade is always i ^ p (reference src/batch_gp.c:127-137).
+// Passed to kernels by value (kernel parameter space, 528 bytes).
+struct SignPlan {
+    uint64_t neg[kMaxBlades];
+    int32_t dimension;
+    int32_t blades;
+    int32_t parameter_on_left;
+    int32_t reserved;
+};
+
+// Sign rule of the reference (src/batch_gp.c:29-45): each axis of `left`
+// flips the sign once per lower axis set in `right`; a shared axis multiplies
+// by its metric entry. Bit-exact integer arithmetic.
+int sign_rule(uint8_t left, uint8_t right, const int8_t *signature, uint8_t dimension);
+bool dimension_valid(unsigned dimension);
+bool signature_valid(const int8_t *signature, unsigned dimension);
+
+// Build the baked plan; returns false for an invalid dimension/signature.
+bool make_sign_plan(SignPlan *out, uint8_t dimension, const int8_t *signature,
+                    int parameter_on_left);
+
+// ---------------------------------------------------------------------------
+// Reduction record written by every CTA of the streaming kernels. The
+// finalize kernel sums records in CTA order, so results are deterministic.
+// Layout per CTA: [0, blades) parameter gradient partial, then:
+constexpr int kRecLoss = 64;      // sum of 0.5 r^2
+constexpr int kRecCheckY = 65;    // sum of 0*y  (NaN iff some y is non-finite)
+constexpr int kRecCheckR = 66;    // sum of 0*r  (NaN iff some r is non-finite)
+constexpr int kRecCheckIn = 67;   // sum of 0*x + 0*t (NaN iff some input is non-finite)
+constexpr int kRecStride = 72;    // doubles per CTA record (576 B, 64-B multiple)
+constexpr int kMaxCtas = 1184;    // 148 SMs x 8
+
+// Status word written by device code (bit flags).
+enum DeviceStatusBits : uint32_t {
+    kDevOk = 0u,
+    kDevInputNonFinite = 1u,     // inputs/targets/parameter not finite
+    kDevOutputNonFinite = 2u,    // forward outputs not finite
+    kDevResidualNonFinite = 4u,  // residual overflowed
+    kDevGradientNonFinite = 8u,  // parameter gradient not finite
+    kDevCandidateNonFinite = 16u,// updated parameter not finite (update not committed)
+    kDevLossNonFinite = 32u,     // mean loss not finite (update committed)
+    kDevBiasInvalid = 64u,       // Adam bias correction not positive/finite
+};
+
+// Optimizer description consumed by the finalize kernel.
+enum OptimizerKind : int32_t {
+    kOptNone = 0,        // gradient + loss only
+    kOptSgdBatchGp = 1,  // w -= lr * g / B        (reference src/batch_gp.c:302-304)
+    kOptSgdV8 = 2,       // w -= lr * (g * scale)  (reference src/full_cycle_v8.c:991,1008)
+    kOptAdamV8 = 3,      // Adam, reference src/full_cycle_v8.c:976-1008
+    kOptSgdScaled = 4,   // w -= (lr / B) * g, unconditional (reference src/batch_gp_cuda.cu:137-140,193-194)
+};
+
+struct OptimizerArgs {
+    int32_t kind;
+    int32_t blades;
+    double learning_rate;
+    double beta1;
+    double beta2;
+    double epsilon;
+    double gradient_scale;   // multiplies the summed gradient (V8 semantics)
+    double batch_divisor;    // B for kOptSgdBatchGp and for the mean loss
+    double bias1;            // 1 - beta1^step, computed on the host with libm pow
+    double bias2;            // 1 - beta2^step
+};
+
+// ---------------------------------------------------------------------------
+// Kernel launchers (kernels_direct.cu). All are asynchronous on `stream` and
+// return the launch error. `records` points to kMaxCtas * kRecStride doubles.
+
+// y = x * W (or W * x): inputs/outputs sample-major [batch][blades].
+cudaError_t launch_forward(const SignPlan &plan, const double *inputs, const double *parameter,
+                           double *outputs, size_t batch, cudaStream_t stream);
+
+// Streaming full cycle. When `targets` is null the kernel only reduces the
+// parameter VJP of `cotangents` (= the r of the loss) against `inputs`.
+//   mode kCycle: r = fwd(x) - t (optionally stored to residuals_out), loss, VJP.
+//   mode kVjp:   VJP of the given cotangents.
+enum CycleMode : int32_t { kCycle = 0, kVjp = 1 };
+cudaError_t launch_cycle(const SignPlan &plan, CycleMode mode, const double *inputs,
+                         const double *targets_or_cotangents, const double *parameter,
+                         double *residuals_out, size_t batch, double *records, int *ctas_used,
+                         cudaStream_t stream);
+
+// Sum `ctas` records in order; write gradient (may be null), loss sum (may be
+// null), apply the optimizer to `parameter` (+ moments for Adam) transactionally
+// and OR status bits into *status (may be null).
+// A non-zero *status on entry blocks the optimizer update (failures chain);
+// `step_counter` (may be null) is incremented on every committed update.
+cudaError_t launch_finalize(const double *records, int ctas, const OptimizerArgs &opt,
+                            double *gradient_out, double *loss_sum_out, double *parameter,
+                            double *first_moment, double *second_moment, uint32_t *status,
+                            cudaStream_t stream, unsigned long long *step_counter = nullptr);
+
+// out[k] = sum over `count` records of record[k], in record order
+// (accumulate != 0: out[k] += that sum).
+cudaError_t launch_reduce_records(const double *records, int count, double *out, cudaStream_t stream,
+                                  int accumulate = 0);
+
+// Finite check of a device array; ORs `bit` into *status when a value is not finite.
+cudaError_t launch_check_finite(const double *values, size_t count, uint32_t bit,
+                                uint32_t *status, cudaStream_t stream);
+
+int device_sm_count();
+
+}  // namespace geo

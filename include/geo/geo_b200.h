@@ -1,0 +1,195 @@
+/*
+ * geo/geo_b200.h -- additive C ABI of libgeo_b200.so (no reference header has
+ * these symbols; each block names the reference code whose semantics it
+ * batches).
+ *
+ *  1. Trainer: a parameter multivector and its optimizer state resident on one
+ *     GPU, trained by the fused full cycle (forward -> residual -> 0.5|r|^2 ->
+ *     parameter VJP -> optimizer) in one streaming pass per minibatch.
+ *     Optimizer semantics are the reference V8 graph runtime's for the graph
+ *     x*w (or w*x) -> add(., scale(t, -1)) -> squared_norm
+ *     (reference src/full_cycle_v8.c:942-1041): g = sum_s grad_s * scale,
+ *     SGD w -= lr g, Adam m = b1 m + (1-b1) g, v = b2 v + (1-b2) g^2,
+ *     w -= lr (m / (1-b1^t)) / (sqrt(v / (1-b2^t)) + eps); transactional
+ *     (nothing changes when any candidate value is non-finite).
+ *  2. Data parallelism: one process (or thread) per GPU; each rank trains on
+ *     its own slice of the global batch and the per-rank gradient/loss record
+ *     (2^n + 8 doubles) is all-gathered over NCCL and summed in rank order, so
+ *     every rank applies the identical update to its replica.
+ *  3. Pairwise products with both operands varying per element (reference
+ *     src/operator_kernel.c:412-539, geo_operator_gp_f64 and its JVP/VJP),
+ *     float64, plus a float32 build of the forward.
+ *  4. Sparse fixed-multivector operators over a batch (reference
+ *     src/operator_kernel.c:191-334, geo_operator_apply_*_f64 and VJPs).
+ *
+ * All device-pointer calls are asynchronous on the given stream; host-pointer
+ * calls are synchronous. Arrays are sample-major [batch][2^n].
+ */
+#ifndef GEO_B200_H
+#define GEO_B200_H
+
+#include "geo/operator_kernel.h"
+
+#include <cuda_runtime_api.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GEO_B200_ABI_VERSION 0x00010000u
+
+typedef enum {
+    GEO_B200_OK = 0,
+    GEO_B200_INVALID_ARGUMENT = 1,
+    GEO_B200_UNSUPPORTED_DIMENSION = 2,
+    GEO_B200_NUMERIC_FAILURE = 3,
+    GEO_B200_RUNTIME_FAILURE = 4,
+    GEO_B200_ALLOCATION_FAILURE = 5,
+    GEO_B200_COMM_FAILURE = 6,
+    GEO_B200_TIMEOUT = 7
+} geo_b200_status_t;
+
+typedef enum {
+    GEO_B200_OPTIMIZER_SGD = 1,  /* same values as GEO_V8_OPTIMIZER_* */
+    GEO_B200_OPTIMIZER_ADAM = 2
+} geo_b200_optimizer_t;
+
+typedef struct {
+    uint32_t optimizer;      /* geo_b200_optimizer_t */
+    double learning_rate;
+    double beta1;
+    double beta2;
+    double epsilon;
+} geo_b200_optimizer_config_t;
+
+typedef struct geo_b200_trainer geo_b200_trainer_t;
+typedef struct geo_b200_comm geo_b200_comm_t;
+
+uint32_t geo_b200_abi_version(void);
+const char *geo_b200_status_string(geo_b200_status_t status);
+
+/* ---- 1. trainer ------------------------------------------------------- */
+
+/* Creates the trainer on the current CUDA device. initial_parameter is a host
+ * array of 2^dimension doubles; moments start at zero and the step count at 0
+ * (like geo_v8_set_value on a PARAMETER, reference src/full_cycle_v8.c:559-563). */
+geo_b200_status_t geo_b200_trainer_create(geo_b200_trainer_t **trainer, uint8_t dimension,
+                                          const int8_t *signature, int parameter_on_left,
+                                          const double *initial_parameter,
+                                          const geo_b200_optimizer_config_t *config);
+void geo_b200_trainer_destroy(geo_b200_trainer_t *trainer);
+
+/* One training step on a device-resident minibatch (inputs/targets
+ * [batch][2^n] in device memory). gradient_scale multiplies the summed
+ * gradient (1/global_batch gives the mean, as geo_v8_optimizer_step's
+ * gradient_scale). Asynchronous on `stream`; numeric status accumulates until
+ * geo_b200_trainer_sync. With a communicator attached, every rank must call it
+ * the same number of times. */
+geo_b200_status_t geo_b200_trainer_step_device(geo_b200_trainer_t *trainer, const double *device_inputs,
+                                               const double *device_targets, size_t batch,
+                                               double gradient_scale, cudaStream_t stream);
+
+/* The two halves of a step, for gradient accumulation over micro-batches
+ * (the batched form of geo_v8_backward(accumulate) + geo_v8_optimizer_step):
+ * accumulate adds the micro-batch's gradient and loss sums to the trainer's
+ * running record; apply reduces the record across ranks (when a communicator
+ * is attached), applies the optimizer with `gradient_scale` and clears the
+ * record. step_device == accumulate + apply. */
+geo_b200_status_t geo_b200_trainer_accumulate_device(geo_b200_trainer_t *trainer, const double *device_inputs,
+                                                     const double *device_targets, size_t batch,
+                                                     cudaStream_t stream);
+geo_b200_status_t geo_b200_trainer_apply(geo_b200_trainer_t *trainer, double gradient_scale, cudaStream_t stream);
+
+/* Same step from host (pageable or pinned) buffers: copies in, trains, waits,
+ * and returns the step's status; *loss_sum receives sum_s 0.5 |r_s|^2 over
+ * the global batch (may be NULL). */
+geo_b200_status_t geo_b200_trainer_step_host(geo_b200_trainer_t *trainer, const double *inputs,
+                                             const double *targets, size_t batch, double gradient_scale,
+                                             double *loss_sum);
+
+/* Waits for all queued steps (bounded by the communicator timeout when one is
+ * attached) and returns the first failure since the previous sync.
+ * *loss_sum (may be NULL) receives the last step's global loss sum. */
+geo_b200_status_t geo_b200_trainer_sync(geo_b200_trainer_t *trainer, double *loss_sum);
+
+/* Host copies of the parameter and Adam moments (any pointer may be NULL). */
+geo_b200_status_t geo_b200_trainer_get_state(geo_b200_trainer_t *trainer, double *parameter,
+                                             double *first_moment, double *second_moment,
+                                             uint64_t *step_count);
+/* Replaces the parameter and resets moments and step count. */
+geo_b200_status_t geo_b200_trainer_set_parameter(geo_b200_trainer_t *trainer, const double *parameter);
+/* Restores a full optimizer state (checkpoint resume). */
+geo_b200_status_t geo_b200_trainer_set_state(geo_b200_trainer_t *trainer, const double *parameter,
+                                             const double *first_moment, const double *second_moment,
+                                             uint64_t step_count);
+/* Device pointer to the resident parameter (2^n doubles). */
+const double *geo_b200_trainer_device_parameter(const geo_b200_trainer_t *trainer);
+
+/* ---- 2. data parallelism ---------------------------------------------- */
+
+#define GEO_B200_COMM_ID_BYTES 128
+
+/* Rank 0 creates the id and shares the bytes with the other ranks out of band. */
+geo_b200_status_t geo_b200_comm_unique_id(unsigned char id[GEO_B200_COMM_ID_BYTES]);
+/* Collective over `world` ranks; uses the current CUDA device. Returns
+ * GEO_B200_TIMEOUT if the ranks have not all joined within timeout_ms. */
+geo_b200_status_t geo_b200_comm_create(geo_b200_comm_t **comm, int rank, int world,
+                                       const unsigned char id[GEO_B200_COMM_ID_BYTES], int timeout_ms);
+void geo_b200_comm_destroy(geo_b200_comm_t *comm);
+/* Aborts in-flight collectives (use after a peer failed). */
+void geo_b200_comm_abort(geo_b200_comm_t *comm);
+geo_b200_status_t geo_b200_trainer_attach_comm(geo_b200_trainer_t *trainer, geo_b200_comm_t *comm);
+
+/* ---- 3. pairwise products (both operands vary per element) ------------ */
+
+/* out[s] = left[s] * right[s]. */
+geo_b200_status_t geo_b200_pairwise_gp_f64(uint8_t dimension, const int8_t *signature, const double *device_left,
+                                           const double *device_right, double *device_out, size_t batch,
+                                           cudaStream_t stream);
+/* Per-element VJP: left_bar[s], right_bar[s] from out_bar[s]
+ * (reference src/operator_kernel.c:494-539). Either output may be NULL. */
+geo_b200_status_t geo_b200_pairwise_gp_vjp_f64(uint8_t dimension, const int8_t *signature,
+                                               const double *device_left, const double *device_right,
+                                               const double *device_out_cotangent, double *device_left_cotangent,
+                                               double *device_right_cotangent, size_t batch, cudaStream_t stream);
+/* Per-element JVP (reference src/operator_kernel.c:449-492). */
+geo_b200_status_t geo_b200_pairwise_gp_jvp_f64(uint8_t dimension, const int8_t *signature,
+                                               const double *device_left, const double *device_right,
+                                               const double *device_left_tangent, const double *device_right_tangent,
+                                               double *device_out_tangent, size_t batch, cudaStream_t stream);
+/* float32 build of the forward. When left_even_compact is non-zero, `left`
+ * holds only the 2^(n-1) even-grade coefficients of each element, in
+ * increasing blade order (compact storage); otherwise 2^n dense values. */
+geo_b200_status_t geo_b200_pairwise_gp_f32(uint8_t dimension, const int8_t *signature, const float *device_left,
+                                           int left_even_compact, const float *device_right, float *device_out,
+                                           size_t batch, cudaStream_t stream);
+
+/* ---- 4. sparse fixed-multivector plans over a batch ------------------- */
+
+/* out[s] = plan applied to in[s] (integer coefficients of the plan). */
+geo_b200_status_t geo_b200_sparse_apply_f64(const geo_operator_plan_i32_t *plan, const double *device_in,
+                                            double *device_out, size_t batch, cudaStream_t stream);
+/* Coefficients replaced by real parameters[term_count] (device array). */
+geo_b200_status_t geo_b200_sparse_apply_parametric_f64(const geo_operator_plan_i32_t *plan,
+                                                       const double *device_parameters, const double *device_in,
+                                                       double *device_out, size_t batch, cudaStream_t stream);
+/* in_bar[s] = M^T out_bar[s] (integer plan). */
+geo_b200_status_t geo_b200_sparse_apply_vjp_f64(const geo_operator_plan_i32_t *plan,
+                                                const double *device_out_cotangent, double *device_in_cotangent,
+                                                size_t batch, cudaStream_t stream);
+/* Parametric VJP: per-element input cotangents (may be NULL) and the
+ * parameter cotangents summed over the batch (term_count doubles, device). */
+geo_b200_status_t geo_b200_sparse_apply_parametric_vjp_f64(const geo_operator_plan_i32_t *plan,
+                                                           const double *device_parameters, const double *device_in,
+                                                           const double *device_out_cotangent,
+                                                           double *device_in_cotangent,
+                                                           double *device_parameter_cotangent, size_t batch,
+                                                           cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

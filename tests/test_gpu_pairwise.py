@@ -1,0 +1,99 @@
+"""GPU parity of pairwise products (both operands vary) and sparse plans."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from geometricelementaryoperators_b200 import abi, canonical_signature
+from geometricelementaryoperators_b200.synthetic import normal, splitmix_uniform
+from tests.conftest import all_signatures, max_violation, tol_close
+from tests.gpu_helpers import TOL, TOL_F32, dev, host, ptr, stream, sync
+
+pytestmark = pytest.mark.gpu
+
+
+def test_pairwise_f64_all_signatures(oracle):
+    L = abi.lib()
+    B = 37
+    for n, q, sig in all_signatures():
+        N = 1 << n
+        a, b, c, ta, tb = (splitmix_uniform(300 + 7 * n + q + k, (B, N)) for k in range(5))
+        da, db, dc, dta, dtb = (dev(v) for v in (a, b, c, ta, tb))
+        out, lb, rb, jt = (dev(np.zeros((B, N))) for _ in range(4))
+        s = abi.sig_array(sig)
+        assert L.geo_b200_pairwise_gp_f64(n, s, ptr(da), ptr(db), ptr(out), B, stream()) == 0
+        assert L.geo_b200_pairwise_gp_vjp_f64(n, s, ptr(da), ptr(db), ptr(dc), ptr(lb), ptr(rb), B, stream()) == 0
+        assert L.geo_b200_pairwise_gp_jvp_f64(n, s, ptr(da), ptr(db), ptr(dta), ptr(dtb), ptr(jt), B, stream()) == 0
+        sync()
+        want = np.stack([oracle.gp(sig, a[i], b[i]) for i in range(B)])
+        assert tol_close(host(out), want, TOL), max_violation(host(out), want, TOL)
+        vj = [oracle.gp_vjp(sig, a[i], b[i], c[i]) for i in range(B)]
+        assert tol_close(host(lb), np.stack([u for u, _ in vj]), TOL)
+        assert tol_close(host(rb), np.stack([v for _, v in vj]), TOL)
+        jv = np.stack([oracle.gp_jvp(sig, a[i], b[i], ta[i], tb[i]) for i in range(B)])
+        assert tol_close(host(jt), jv, TOL)
+
+
+@pytest.mark.parametrize("compact", [0, 1])
+def test_pairwise_f32_even_operand(oracle, compact):
+    """Cl(6,0) float32 build: even-grade left operand (32 blades, N(0,1)), dense right U[-1,1];
+    float64 oracle at 1e-5."""
+    import torch
+
+    L = abi.lib()
+    sig = canonical_signature(6, 0)
+    B = 3001
+    even = np.array([b for b in range(64) if bin(b).count("1") % 2 == 0])
+    a = np.zeros((B, 64))
+    a[:, even] = normal(61, (B, 32))
+    b = splitmix_uniform(62, (B, 64))
+    a32 = a.astype(np.float32)
+    b32 = b.astype(np.float32)
+    left = a32[:, even] if compact else a32
+    dl = torch.from_numpy(np.ascontiguousarray(left)).cuda()
+    dr = torch.from_numpy(b32).cuda()
+    out = torch.zeros((B, 64), dtype=torch.float32, device="cuda")
+    assert L.geo_b200_pairwise_gp_f32(6, abi.sig_array(sig), ptr(dl), compact, ptr(dr), ptr(out), B, stream()) == 0
+    sync()
+    want = np.stack([oracle.gp(sig, a32[i].astype(np.float64), b32[i].astype(np.float64)) for i in range(B)])
+    got = host(out).astype(np.float64)
+    assert tol_close(got, want, TOL_F32), max_violation(got, want, TOL_F32)
+
+
+def test_sparse_plans(oracle):
+    L = abi.lib()
+    B = 129
+    for n, q, sig in all_signatures(2, 6):
+        N = 1 << n
+        rng = np.random.default_rng(n * 10 + q)
+        k = min(N, 6)
+        blades = rng.choice(N, size=k, replace=False)
+        coeffs = rng.integers(1, 4, size=k) * rng.choice([-1, 1], size=k)
+        params = rng.uniform(-2, 2, k)
+        x = splitmix_uniform(500 + n + q, (B, N))
+        c = splitmix_uniform(600 + n + q, (B, N))
+        dx, dc, dp = dev(x), dev(c), dev(params)
+        for side in (0, 1):
+            plan = abi.OperatorPlanI32()
+            terms = (abi.OperatorTermI32 * k)(*[abi.OperatorTermI32(int(b), int(cf)) for b, cf in zip(blades, coeffs)])
+            assert L.geo_operator_plan_sparse_i32(ctypes.byref(plan), n, abi.sig_array(sig), side, terms, k) == 0
+            o1, o2, o3, o4 = (dev(np.zeros((B, N))) for _ in range(4))
+            pc = dev(np.zeros(k))
+            assert L.geo_b200_sparse_apply_f64(ctypes.byref(plan), ptr(dx), ptr(o1), B, stream()) == 0
+            assert L.geo_b200_sparse_apply_parametric_f64(ctypes.byref(plan), ptr(dp), ptr(dx), ptr(o2), B,
+                                                          stream()) == 0
+            assert L.geo_b200_sparse_apply_vjp_f64(ctypes.byref(plan), ptr(dc), ptr(o3), B, stream()) == 0
+            assert L.geo_b200_sparse_apply_parametric_vjp_f64(ctypes.byref(plan), ptr(dp), ptr(dx), ptr(dc), ptr(o4),
+                                                              ptr(pc), B, stream()) == 0
+            sync()
+            assert tol_close(host(o1), np.stack([oracle.sparse_apply(sig, side, blades, coeffs, x[i])
+                                                 for i in range(B)]), TOL)
+            assert tol_close(host(o2), np.stack([oracle.sparse_apply_parametric(sig, side, blades, params, x[i])
+                                                 for i in range(B)]), TOL)
+            assert tol_close(host(o3), np.stack([oracle.sparse_apply_vjp(sig, side, blades, coeffs, c[i])
+                                                 for i in range(B)]), TOL)
+            pv = [oracle.sparse_apply_parametric_vjp(sig, side, blades, params, x[i], c[i]) for i in range(B)]
+            assert tol_close(host(o4), np.stack([u for u, _ in pv]), TOL)
+            assert tol_close(host(pc), np.sum(np.stack([v for _, v in pv]), axis=0), TOL)
