@@ -162,8 +162,13 @@ def make_data(lib, sig, batch, seed, left=0):
     return X, T, w0.numpy()
 
 
+ALGORITHM_NAMES = {1: "cayley", 2: "representation"}
+KERNEL_NAMES = {1: "tiled_kernel<64, cycle> (Cayley matrix, FP64 FMA)",
+                2: "rep_cycle_kernel (D x D representation, FP64 tensor cores)"}
+
+
 class Trainer:
-    def __init__(self, lib, sig, w0, left=0):
+    def __init__(self, lib, sig, w0, left=0, algorithm=0):
         from geometricelementaryoperators_b200 import abi
 
         self.lib = lib
@@ -176,6 +181,9 @@ class Trainer:
                                          self.w0.ctypes.data_as(ctypes.c_void_p), ctypes.byref(cfg))
         if st != 0:
             raise RuntimeError(f"trainer_create failed: {st}")
+        if algorithm:
+            assert lib.geo_b200_trainer_set_algorithm(self.h, algorithm) == 0
+        self.algorithm = lib.geo_b200_trainer_algorithm(self.h)
 
     def destroy(self):
         self.lib.geo_b200_trainer_destroy(self.h)
@@ -349,6 +357,30 @@ def run_b200(args, world, rank, local):
 
     extras = {}
     if not args.no_extras:
+        # The other kernel family on the same data, for comparison.
+        other = 1 if tr.algorithm == 2 else 2
+        try:
+            trc = Trainer(lib, sig, w0, algorithm=other)
+        except AssertionError:
+            trc = None
+        if trc is not None:
+            if world > 1:
+                assert lib.geo_b200_trainer_attach_comm(trc.h, comm) == 0
+            for _ in range(args.warmup):
+                assert lib.geo_b200_trainer_step_device(trc.h, xp, tp, batch, scale, sp) == 0
+            torch.cuda.synchronize()
+            barrier(world)
+            sc, ec = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            sc.record(stream)
+            for _ in range(args.steps):
+                assert lib.geo_b200_trainer_step_device(trc.h, xp, tp, batch, scale, sp) == 0
+            ec.record(stream)
+            torch.cuda.synchronize()
+            assert lib.geo_b200_trainer_sync(trc.h, None) == 0
+            msc = max_over_ranks(sc.elapsed_time(ec) / args.steps, world)
+            extras["other_algorithm"] = {"algorithm": ALGORITHM_NAMES[other],
+                                         "value": batch * world / (msc / 1e3), "ms_per_step": msc}
+            trc.destroy()
         # Same step on Cl(3,3) (the second signature of the headline config).
         X2, T2, w2 = X, T, w0
         tr33 = Trainer(lib, [1, 1, 1, -1, -1, -1], w2)
@@ -394,7 +426,7 @@ def run_b200(args, world, rank, local):
     achieved = algo_bytes / (kernel_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                 "frac": achieved / hbm_peak, "traffic": None, "peak_source": peak_src,
-                "kernel": "tiled_kernel<64, cycle> (+ record reduction) per step, CUDA events on the launch stream",
+                "kernel": KERNEL_NAMES[tr.algorithm] + " + record reduction, CUDA events on the launch stream",
                 "kernel_ms": kernel_ms,
                 "fp64_flops_achieved_tflops": batch * FLOPS_PER_SAMPLE / (kernel_ms / 1e3) / 1e12}
     if rank == 0:
@@ -412,7 +444,10 @@ def run_b200(args, world, rank, local):
             "gpu_launches": args.steps * 3,
             "clocks": clock_info,
             "final_loss_sum": loss.value,
+            "algorithm": ALGORITHM_NAMES[tr.algorithm],
         }
+        if "other_algorithm" in extras:
+            line["other_algorithm"] = extras["other_algorithm"]
         if "e2e" in extras:
             line["e2e"] = extras["e2e"]
         if "cl33" in extras:

@@ -136,6 +136,8 @@ SIGNATURES: dict[str, tuple] = {
     "geo_b200_trainer_set_parameter": (_I, [_P, _P]),
     "geo_b200_trainer_set_state": (_I, [_P, _P, _P, _P, ctypes.c_uint64]),
     "geo_b200_trainer_device_parameter": (_P, [_P]),
+    "geo_b200_trainer_set_algorithm": (_I, [_P, _I]),
+    "geo_b200_trainer_algorithm": (_I, [_P]),
     "geo_b200_comm_unique_id": (_I, [_P]),
     "geo_b200_comm_create": (_I, [ctypes.POINTER(_P), _I, _I, _P, _I]),
     "geo_b200_comm_destroy": (None, [_P]),

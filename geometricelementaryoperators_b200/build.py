@@ -2,8 +2,8 @@
 
 Every CUDA/C++ source under csrc/ is compiled by nvcc with
 ``-gencode arch=compute_100a,code=sm_100a -lineinfo`` into _build/, then linked
-into ``geometricelementaryoperators_b200/libgeo_b200.so`` (static CUDA runtime,
-dynamic NCCL). Objects are rebuilt only when a source or header is newer.
+into ``geometricelementaryoperators_b200/libgeo_b200.so`` (static CUDA runtime;
+NCCL is opened at run time when a communicator is created). Objects are rebuilt only when a source or header is newer.
 
 Usage: ``python -m geometricelementaryoperators_b200.build [-v] [--force]``.
 """
@@ -73,7 +73,7 @@ def build(verbose: bool = False, force: bool = False, extra_flags: list[str] | N
     with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
         list(ex.map(lambda j: _compile(j[0], j[1], verbose), jobs))
     if jobs or force or not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lnccl", "-lpthread"]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-ldl", "-lpthread"]
         if verbose:
             print(" ".join(cmd), flush=True)
         res = subprocess.run(cmd, capture_output=True, text=True)

@@ -14,8 +14,9 @@
 // (a 576-byte message) and every rank sums them in rank order before the
 // identical update, so replicas stay bit-identical without a broadcast.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 #include <math.h>
-#include <nccl.h>
+#include <nccl.h>  // types and NCCL_CONFIG_INITIALIZER only; entry points are resolved at run time
 #include <string.h>
 
 #include <chrono>
@@ -24,6 +25,7 @@
 
 #include "geo/geo_b200.h"
 #include "geo_runtime.h"
+#include "representation.h"
 
 struct geo_b200_comm {
     ncclComm_t comm = nullptr;
@@ -36,6 +38,9 @@ struct geo_b200_comm {
 struct geo_b200_trainer {
     int device = 0;
     geo::SignPlan plan;
+    geo::RepDevice rep;
+    bool rep_ok = false;
+    int algorithm = GEO_B200_ALGORITHM_AUTO;
     int blades = 0;
     geo_b200_optimizer_config_t config;
     double *state = nullptr;     // [0,64) w, [64,128) m, [128,192) v, [192] loss sum, [200,272) rank record
@@ -54,6 +59,43 @@ struct geo_b200_trainer {
 };
 
 namespace {
+
+// NCCL is resolved lazily with dlopen when the first communicator is made, so
+// loading libgeo_b200.so never pulls an NCCL into the process: a host program
+// (or a framework loaded later) keeps whichever NCCL it links itself, and an
+// NCCL already present in the process is reused.
+struct NcclApi {
+    bool loaded = false;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+};
+
+NcclApi load_nccl() {
+    NcclApi api;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (h == nullptr) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h == nullptr) return api;
+    api.GetUniqueId = (decltype(api.GetUniqueId))dlsym(h, "ncclGetUniqueId");
+    api.CommInitRankConfig = (decltype(api.CommInitRankConfig))dlsym(h, "ncclCommInitRankConfig");
+    api.CommGetAsyncError = (decltype(api.CommGetAsyncError))dlsym(h, "ncclCommGetAsyncError");
+    api.CommAbort = (decltype(api.CommAbort))dlsym(h, "ncclCommAbort");
+    api.CommFinalize = (decltype(api.CommFinalize))dlsym(h, "ncclCommFinalize");
+    api.CommDestroy = (decltype(api.CommDestroy))dlsym(h, "ncclCommDestroy");
+    api.AllGather = (decltype(api.AllGather))dlsym(h, "ncclAllGather");
+    api.loaded = api.GetUniqueId && api.CommInitRankConfig && api.CommGetAsyncError && api.CommAbort &&
+                 api.CommFinalize && api.CommDestroy && api.AllGather;
+    return api;
+}
+
+NcclApi &nccl() {
+    static NcclApi api = load_nccl();  // thread-safe one-time initialisation
+    return api;
+}
 
 constexpr size_t kStateW = 0, kStateM = 64, kStateV = 128, kStateLoss = 192, kStateRecord = 200;
 constexpr size_t kStateDoubles = kStateRecord + geo::kRecStride;
@@ -81,7 +123,7 @@ geo_b200_status_t wait_stream(cudaStream_t stream, geo_b200_comm_t *comm) {
         if (q == cudaSuccess) return GEO_B200_OK;
         if (q != cudaErrorNotReady) return from_cuda(q);
         ncclResult_t async = ncclSuccess;
-        if (ncclCommGetAsyncError(comm->comm, &async) != ncclSuccess ||
+        if (nccl().CommGetAsyncError(comm->comm, &async) != ncclSuccess ||
             (async != ncclSuccess && async != ncclInProgress)) {
             geo_b200_comm_abort(comm);
             return GEO_B200_COMM_FAILURE;
@@ -104,7 +146,7 @@ geo_b200_status_t nccl_settle(geo_b200_comm_t *comm, ncclResult_t r) {
     const auto start = std::chrono::steady_clock::now();
     for (;;) {
         ncclResult_t async = ncclInProgress;
-        if (ncclCommGetAsyncError(comm->comm, &async) != ncclSuccess) return GEO_B200_COMM_FAILURE;
+        if (nccl().CommGetAsyncError(comm->comm, &async) != ncclSuccess) return GEO_B200_COMM_FAILURE;
         if (async == ncclSuccess) return GEO_B200_OK;
         if (async != ncclInProgress) return GEO_B200_COMM_FAILURE;
         const auto waited =
@@ -156,6 +198,11 @@ extern "C" geo_b200_status_t geo_b200_trainer_create(geo_b200_trainer_t **out, u
     }
     t->blades = blades;
     t->config = *config;
+    {
+        geo::RepPlan rp;
+        t->rep_ok = geo::make_rep_plan(&rp, dimension, signature, parameter_on_left) &&
+                    geo::make_rep_device(&t->rep, rp) && geo::rep_supported(t->rep);
+    }
     cudaGetDevice(&t->device);
     geo_b200_status_t st = GEO_B200_OK;
     double init[kStateDoubles];
@@ -202,8 +249,13 @@ extern "C" geo_b200_status_t geo_b200_trainer_accumulate_device(geo_b200_trainer
     if (t == nullptr || device_inputs == nullptr || device_targets == nullptr || batch == 0)
         return GEO_B200_INVALID_ARGUMENT;
     int ctas = 0;
-    cudaError_t e = geo::launch_cycle(t->plan, geo::kCycle, device_inputs, device_targets, t->state + kStateW,
-                                      nullptr, batch, t->records, &ctas, stream);
+    cudaError_t e;
+    if (geo_b200_trainer_algorithm(t) == GEO_B200_ALGORITHM_REPRESENTATION)
+        e = geo::launch_rep_cycle(t->rep, device_inputs, device_targets, t->state + kStateW, batch, t->records, &ctas,
+                                  stream);
+    else
+        e = geo::launch_cycle(t->plan, geo::kCycle, device_inputs, device_targets, t->state + kStateW, nullptr,
+                              batch, t->records, &ctas, stream);
     if (e == cudaSuccess) e = geo::launch_reduce_records(t->records, ctas, t->state + kStateRecord, stream, 1);
     t->last_stream = stream;
     return from_cuda(e);
@@ -236,7 +288,7 @@ extern "C" geo_b200_status_t geo_b200_trainer_apply(geo_b200_trainer_t *t, doubl
     if (t->comm != nullptr && t->comm->world > 1) {
         if (t->comm->aborted) return GEO_B200_COMM_FAILURE;
         const geo_b200_status_t s = nccl_settle(
-            t->comm, ncclAllGather(t->state + kStateRecord, t->gather, (size_t)geo::kRecStride, ncclDouble,
+            t->comm, nccl().AllGather(t->state + kStateRecord, t->gather, (size_t)geo::kRecStride, ncclDouble,
                                    t->comm->comm, stream));
         if (s != GEO_B200_OK) return s;
         final_records = t->gather;
@@ -364,6 +416,23 @@ extern "C" geo_b200_status_t geo_b200_trainer_set_parameter(geo_b200_trainer_t *
     return geo_b200_trainer_set_state(t, parameter, nullptr, nullptr, 0u);
 }
 
+extern "C" geo_b200_status_t geo_b200_trainer_set_algorithm(geo_b200_trainer_t *t, geo_b200_algorithm_t algorithm) {
+    if (t == nullptr) return GEO_B200_INVALID_ARGUMENT;
+    if (algorithm != GEO_B200_ALGORITHM_AUTO && algorithm != GEO_B200_ALGORITHM_CAYLEY &&
+        algorithm != GEO_B200_ALGORITHM_REPRESENTATION)
+        return GEO_B200_INVALID_ARGUMENT;
+    if (algorithm == GEO_B200_ALGORITHM_REPRESENTATION && !t->rep_ok) return GEO_B200_INVALID_ARGUMENT;
+    t->algorithm = algorithm;
+    return GEO_B200_OK;
+}
+
+extern "C" geo_b200_algorithm_t geo_b200_trainer_algorithm(const geo_b200_trainer_t *t) {
+    if (t == nullptr) return GEO_B200_ALGORITHM_AUTO;
+    if (t->algorithm == GEO_B200_ALGORITHM_CAYLEY) return GEO_B200_ALGORITHM_CAYLEY;
+    if (t->algorithm == GEO_B200_ALGORITHM_REPRESENTATION) return GEO_B200_ALGORITHM_REPRESENTATION;
+    return (t->rep_ok && t->plan.dimension >= 5) ? GEO_B200_ALGORITHM_REPRESENTATION : GEO_B200_ALGORITHM_CAYLEY;
+}
+
 extern "C" const double *geo_b200_trainer_device_parameter(const geo_b200_trainer_t *t) {
     return t == nullptr ? nullptr : t->state + kStateW;
 }
@@ -374,8 +443,9 @@ static_assert(sizeof(ncclUniqueId) == GEO_B200_COMM_ID_BYTES, "NCCL unique id si
 
 extern "C" geo_b200_status_t geo_b200_comm_unique_id(unsigned char id[GEO_B200_COMM_ID_BYTES]) {
     if (id == nullptr) return GEO_B200_INVALID_ARGUMENT;
+    if (!nccl().loaded) return GEO_B200_COMM_FAILURE;
     ncclUniqueId uid;
-    if (ncclGetUniqueId(&uid) != ncclSuccess) return GEO_B200_COMM_FAILURE;
+    if (nccl().GetUniqueId(&uid) != ncclSuccess) return GEO_B200_COMM_FAILURE;
     memcpy(id, &uid, sizeof(uid));
     return GEO_B200_OK;
 }
@@ -385,6 +455,7 @@ extern "C" geo_b200_status_t geo_b200_comm_create(geo_b200_comm_t **out, int ran
     if (out == nullptr || id == nullptr || world < 1 || rank < 0 || rank >= world || timeout_ms <= 0)
         return GEO_B200_INVALID_ARGUMENT;
     *out = nullptr;
+    if (!nccl().loaded) return GEO_B200_COMM_FAILURE;
     geo_b200_comm_t *c = new (std::nothrow) geo_b200_comm_t();
     if (c == nullptr) return GEO_B200_ALLOCATION_FAILURE;
     c->rank = rank;
@@ -394,7 +465,7 @@ extern "C" geo_b200_status_t geo_b200_comm_create(geo_b200_comm_t **out, int ran
     memcpy(&uid, id, sizeof(uid));
     ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
     config.blocking = 0;
-    ncclResult_t r = ncclCommInitRankConfig(&c->comm, world, uid, rank, &config);
+    ncclResult_t r = nccl().CommInitRankConfig(&c->comm, world, uid, rank, &config);
     geo_b200_status_t st = GEO_B200_OK;
     if (r == ncclInProgress || r == ncclSuccess) {
         st = nccl_settle(c, r == ncclSuccess ? ncclInProgress : r);
@@ -402,7 +473,7 @@ extern "C" geo_b200_status_t geo_b200_comm_create(geo_b200_comm_t **out, int ran
         st = GEO_B200_COMM_FAILURE;
     }
     if (st != GEO_B200_OK) {
-        if (c->comm != nullptr) ncclCommAbort(c->comm);
+        if (c->comm != nullptr) nccl().CommAbort(c->comm);
         delete c;
         return st;
     }
@@ -412,16 +483,16 @@ extern "C" geo_b200_status_t geo_b200_comm_create(geo_b200_comm_t **out, int ran
 
 extern "C" void geo_b200_comm_abort(geo_b200_comm_t *c) {
     if (c == nullptr || c->comm == nullptr || c->aborted) return;
-    ncclCommAbort(c->comm);
+    nccl().CommAbort(c->comm);
     c->aborted = true;
 }
 
 extern "C" void geo_b200_comm_destroy(geo_b200_comm_t *c) {
     if (c == nullptr) return;
     if (c->comm != nullptr && !c->aborted) {
-        ncclResult_t r = ncclCommFinalize(c->comm);
+        ncclResult_t r = nccl().CommFinalize(c->comm);
         if (r == ncclInProgress) (void)nccl_settle(c, r);
-        ncclCommDestroy(c->comm);
+        nccl().CommDestroy(c->comm);
     }
     delete c;
 }

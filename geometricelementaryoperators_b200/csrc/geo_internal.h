@@ -124,4 +124,24 @@ cudaError_t launch_check_finite(const double *values, size_t count, uint32_t bit
 
 int device_sm_count();
 
+// ---------------------------------------------------------------------------
+// Representation path (kernels_rep.cu, representation.h): fused training pass
+// through a D x D real matrix representation on FP64 tensor cores.
+struct RepPlan;
+struct RepDevice {
+    uint8_t xm[64];
+    uint8_t zm[64];
+    int8_t sg[64];
+    uint8_t gb[8][64];   // [term][kept entry] blade
+    int8_t gs[8][64];    // [term][kept entry] sign
+    int32_t blades, D, S, side;
+};
+bool make_rep_device(RepDevice *out, const RepPlan &plan);
+// True when a tensor-core kernel exists for the plan's (D, S).
+bool rep_supported(const RepDevice &rep);
+// Same record contract as launch_cycle(kCycle) without residual output.
+cudaError_t launch_rep_cycle(const RepDevice &rep, const double *inputs, const double *targets,
+                             const double *parameter, size_t batch, double *records, int *ctas_used,
+                             cudaStream_t stream);
+
 }  // namespace geo

@@ -401,24 +401,49 @@ small_kernel(const SignPlan plan, const double *__restrict__ in, const double *_
 }
 
 // ---------------------------------------------------------------------------
+// Ordered sum of `count` records into totals[kRecStride] with kRecThreads
+// threads: thread (slot, part) sums a contiguous chunk of records, then the
+// kRecParts chunk sums are added in chunk order. Deterministic.
+constexpr int kRecParts = 8;
+constexpr int kRecThreads = kRecStride * kRecParts;  // 576
+
+__device__ __forceinline__ void ordered_record_sum(const double *__restrict__ records, int count,
+                                                   double *totals /* smem kRecStride */,
+                                                   double *parts /* smem kRecThreads */) {
+    const int t = threadIdx.x;
+    if (t < kRecThreads) {
+        const int slot = t % kRecStride;
+        const int part = t / kRecStride;
+        const int chunk = (count + kRecParts - 1) / kRecParts;
+        const int lo = part * chunk;
+        const int hi = min(count, lo + chunk);
+        double acc = 0.0;
+        for (int c = lo; c < hi; ++c) acc += records[(size_t)c * kRecStride + slot];
+        parts[part * kRecStride + slot] = acc;
+    }
+    __syncthreads();
+    if (t < kRecStride) {
+        double acc = 0.0;
+        for (int p = 0; p < kRecParts; ++p) acc += parts[p * kRecStride + t];
+        totals[t] = acc;
+    }
+    __syncthreads();
+}
+
 // Finalize: ordered sum of CTA records, status probes, optimizer (transactional).
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(kRecThreads)
 finalize_kernel(const double *__restrict__ records, int ctas, const OptimizerArgs opt,
                 double *__restrict__ gradient_out, double *__restrict__ loss_sum_out,
                 double *__restrict__ parameter, double *__restrict__ first_moment,
                 double *__restrict__ second_moment, uint32_t *__restrict__ status,
                 unsigned long long *__restrict__ step_counter) {
     __shared__ double totals[kRecStride];
+    __shared__ double parts[kRecThreads];
     // A failure recorded by an earlier step on this stream blocks later updates
     // until the host clears the status word (transactional chain).
     const bool blocked = status != nullptr && opt.kind != kOptNone && opt.kind != kOptSgdScaled && *status != 0u;
     const int t = threadIdx.x;
-    if (t < kRecStride) {
-        double acc = 0.0;
-        for (int c = 0; c < ctas; ++c) acc += records[(size_t)c * kRecStride + t];
-        totals[t] = acc;
-    }
-    __syncthreads();
+    ordered_record_sum(records, ctas, totals, parts);
     const int blades = opt.blades;
     const double loss = totals[kRecLoss];
     const bool bad_y = !isfinite(totals[kRecCheckY]);
@@ -483,14 +508,13 @@ finalize_kernel(const double *__restrict__ records, int ctas, const OptimizerArg
     if (t == 0 && status != nullptr && bits != 0u) atomicOr(status, bits);
 }
 
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(kRecThreads)
 reduce_records_kernel(const double *__restrict__ records, int count, double *__restrict__ out, int accumulate) {
+    __shared__ double totals[kRecStride];
+    __shared__ double parts[kRecThreads];
+    ordered_record_sum(records, count, totals, parts);
     const int t = threadIdx.x;
-    if (t < kRecStride) {
-        double acc = 0.0;
-        for (int c = 0; c < count; ++c) acc += records[(size_t)c * kRecStride + t];
-        out[t] = accumulate ? out[t] + acc : acc;
-    }
+    if (t < kRecStride) out[t] = accumulate ? out[t] + totals[t] : totals[t];
 }
 
 __global__ void check_finite_kernel(const double *__restrict__ values, size_t count, uint32_t bit,
@@ -593,14 +617,14 @@ cudaError_t launch_cycle(const SignPlan &plan, CycleMode mode, const double *inp
 cudaError_t launch_finalize(const double *records, int ctas, const OptimizerArgs &opt, double *gradient_out,
                             double *loss_sum_out, double *parameter, double *first_moment, double *second_moment,
                             uint32_t *status, cudaStream_t stream, unsigned long long *step_counter) {
-    finalize_kernel<<<1, 128, 0, stream>>>(records, ctas, opt, gradient_out, loss_sum_out, parameter, first_moment,
+    finalize_kernel<<<1, kRecThreads, 0, stream>>>(records, ctas, opt, gradient_out, loss_sum_out, parameter, first_moment,
                                            second_moment, status, step_counter);
     return cudaGetLastError();
 }
 
 cudaError_t launch_reduce_records(const double *records, int count, double *out, cudaStream_t stream,
                                   int accumulate) {
-    reduce_records_kernel<<<1, 128, 0, stream>>>(records, count, out, accumulate);
+    reduce_records_kernel<<<1, kRecThreads, 0, stream>>>(records, count, out, accumulate);
     return cudaGetLastError();
 }
 

@@ -1,0 +1,371 @@
+// kernels_rep.cu -- fused training pass on FP64 tensor cores through a real
+// matrix representation of the algebra (see representation.h).
+//
+// Per sample s (2^n blades, S kept rows of a D x D representation, S*D = 2^n):
+//   X'_s = P x_s,  T'_s = P t_s              signed gathers (S terms each)
+//   Y'_s = X'_s W',  R'_s = Y'_s - T'_s       S x D times D x D   (GEMM 1)
+//   loss += |R'_s|^2 / (2S)
+//   G'  += X'_s^T R'_s                         D x D, reduced over the batch (GEMM 2)
+// and once per CTA: g_A = <G', rho(e_A)> / S (or rho(e_A)^T for the left side).
+// This is the reference's forward -> residual -> 0.5 r^2 -> parameter VJP
+// (src/batch_gp.c:237-308) with the 4^n-term Cayley product replaced by an
+// S*D*D GEMM: Cl(6,0)-type algebras use D = 16, S = 4 (1024 multiply-adds per
+// GEMM per sample instead of 4096), Cl(3,3)-type D = 8, S = 8 (512).
+//
+// Both GEMMs run on FP64 tensor cores with mma.sync.aligned.m16n8k4 (16-row
+// blocks of X' = 16/S samples per warp step; W' fragments stay in registers for
+// the whole kernel). GEMM 2 reads X'^T directly from shared memory as the A
+// operand, so no transpose is materialised. The signed gathers run on the FP64
+// pipe while other warps issue tensor-core work.
+//
+// HBM traffic per step = 2 x 8 x 2^n bytes per sample (x and t read once);
+// the padded shared-memory rows (D + 4 doubles) keep every fragment load at
+// two wavefronts.
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "geo_internal.h"
+#include "representation.h"
+
+namespace geo {
+
+bool make_rep_device(RepDevice *out, const RepPlan &p) {
+    if (!p.valid) return false;
+    for (int A = 0; A < 64; ++A) {
+        out->xm[A] = p.xm[A];
+        out->zm[A] = p.zm[A];
+        out->sg[A] = p.sg[A];
+    }
+    for (int t = 0; t < 8; ++t)
+        for (int e = 0; e < 64; ++e) {
+            out->gb[t][e] = t < p.c ? p.gb[e][t] : 0;
+            out->gs[t][e] = t < p.c ? p.gs[e][t] : 0;
+        }
+    out->blades = p.blades;
+    out->D = p.D;
+    out->S = p.S;
+    out->side = p.side;
+    return true;
+}
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = 8;
+
+__device__ __forceinline__ void cp_async_16(void *smem, const void *gmem, int src_bytes) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_8(void *smem, const void *gmem, int src_bytes) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int Pending>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(Pending) : "memory");
+}
+
+// D(16x8) += A(16x4) * B(4x8), float64 tensor cores.
+// Fragments (g = lane / 4, t = lane % 4): a0 = A[g][t], a1 = A[g+8][t];
+// b0 = B[t][g]; c0,c1 = C[g][2t, 2t+1], c2,c3 = C[g+8][2t, 2t+1].
+__device__ __forceinline__ void mma_16x8x4(double (&c)[4], double a0, double a1, double b0) {
+    asm volatile("mma.sync.aligned.m16n8k4.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+                 : "+d"(c[0]), "+d"(c[1]), "+d"(c[2]), "+d"(c[3])
+                 : "d"(a0), "d"(a1), "d"(b0));
+}
+
+template <int D, int S>
+struct RepGeo {
+    static constexpr int N = D * S;         // blades
+    static constexpr int LD = D + 4;        // padded row stride of X', T'/R' (doubles)
+    static constexpr int TS = (D == 8 && S == 8) ? 24 : 32;  // samples per tile (2 CTAs per SM fit)
+    static constexpr int ROWS = TS * S;     // X' rows per tile
+    static constexpr int BLOCKS = ROWS / 16;
+    static constexpr int NT = D / 8;        // 8-column tiles of the D outputs
+    static constexpr int KT = D / 4;        // k-steps of GEMM 1
+    static constexpr int RAW = TS * N;      // doubles of one raw tile
+    static_assert(ROWS % 16 == 0 && D % 8 == 0, "tile shape");
+};
+
+template <int N, int TS, bool AL>
+__device__ __forceinline__ void stage_raw(double *dst, const double *__restrict__ src, size_t first, size_t batch) {
+    if (AL) {
+        for (int c = threadIdx.x; c < TS * (N / 2); c += kThreads) {
+            const int s = c / (N / 2);
+            const size_t sample = first + (size_t)s;
+            const bool ok = sample < batch;
+            const double *g = ok ? src + first * N + 2 * (size_t)c : src;
+            cp_async_16(dst + 2 * c, g, ok ? 16 : 0);
+        }
+    } else {
+        for (int c = threadIdx.x; c < TS * N; c += kThreads) {
+            const int s = c / N;
+            const size_t sample = first + (size_t)s;
+            const bool ok = sample < batch;
+            const double *g = ok ? src + first * N + (size_t)c : src;
+            cp_async_8(dst + c, g, ok ? 8 : 0);
+        }
+    }
+}
+
+// X'[(s*S + r) * LD + k] = sum_t gs[t][e] raw[s*N + gb[t][e]],  e = r*D + k.
+template <int D, int S>
+__device__ __forceinline__ void gather(double *dst, const double *raw, const uint8_t *gb, const int8_t *gs) {
+    using G = RepGeo<D, S>;
+    for (int idx = threadIdx.x; idx < G::TS * G::N; idx += kThreads) {
+        const int s = idx / G::N;
+        const int e = idx - s * G::N;
+        const double *row = raw + s * G::N;
+        double acc = 0.0;
+#pragma unroll
+        for (int t = 0; t < S; ++t) {
+            const double v = row[gb[t * 64 + e]];
+            acc = gs[t * 64 + e] > 0 ? acc + v : acc - v;
+        }
+        const int r = e / D;
+        const int k = e - r * D;
+        dst[(s * S + r) * G::LD + k] = acc;
+    }
+}
+
+template <int D, int S, bool AL>
+__global__ void __launch_bounds__(kThreads, 2)
+rep_cycle_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ T,
+                 const double *__restrict__ W, size_t batch, double *__restrict__ records) {
+    using G = RepGeo<D, S>;
+    constexpr int N = G::N, LD = G::LD, TS = G::TS;
+    extern __shared__ __align__(16) double smem[];
+    double *Wp = smem;                              // D*D
+    double *Xp = Wp + D * D;                        // ROWS*LD
+    double *Tp = Xp + G::ROWS * LD;                 // ROWS*LD (T', then R')
+    double *raw = Tp + G::ROWS * LD;                // 2 stages x (x tile, t tile)
+    __shared__ uint8_t gb[8 * 64];
+    __shared__ int8_t gs[8 * 64];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t4 = lane & 3;
+
+    for (int i = threadIdx.x; i < 8 * 64; i += kThreads) {
+        gb[i] = rep.gb[i / 64][i % 64];
+        gs[i] = rep.gs[i / 64][i % 64];
+    }
+    // W' = rho(W) (right) or rho(W)^T (left): W'[k][j] = sum_{A: x_A = k^j} W_A sg_A (-1)^{z_A . col}
+    for (int idx = threadIdx.x; idx < D * D; idx += kThreads) {
+        const int k = idx / D, j = idx - k * D;
+        const int col = rep.side ? k : j;
+        double acc = 0.0;
+        for (int A = 0; A < N; ++A) {
+            if (rep.xm[A] != (k ^ j)) continue;
+            const double w = W[A];
+            const bool neg = (rep.sg[A] < 0) != ((__popc(rep.zm[A] & col) & 1) != 0);
+            acc += neg ? -w : w;
+        }
+        Wp[idx] = acc;
+    }
+
+    const size_t tiles = (batch + TS - 1) / TS;
+    size_t tile = blockIdx.x;
+    if (tile < tiles) {
+        stage_raw<N, TS, AL>(raw, X, tile * TS, batch);
+        stage_raw<N, TS, AL>(raw + G::RAW, T, tile * TS, batch);
+    }
+    cp_async_commit();
+    __syncthreads();
+
+    // W' fragments for GEMM 1 (B operand, k-steps x n-tiles), resident all kernel.
+    double bw[G::KT][G::NT];
+#pragma unroll
+    for (int kt = 0; kt < G::KT; ++kt)
+#pragma unroll
+        for (int nt = 0; nt < G::NT; ++nt) bw[kt][nt] = Wp[(kt * 4 + t4) * D + nt * 8 + g];
+
+    // G' accumulators (this warp's partial): M = D rows in 16-row tiles, N = D cols in 8-col tiles.
+    constexpr int MT = (D + 15) / 16;  // 1 for D = 8 or 16 (D = 8 uses the top half only)
+    double gacc[MT][G::NT][4];
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int nt = 0; nt < G::NT; ++nt) gacc[m][nt][0] = gacc[m][nt][1] = gacc[m][nt][2] = gacc[m][nt][3] = 0.0;
+    double sq = 0.0, check_y = 0.0, check_r = 0.0;
+
+    int stage = 0;
+    for (; tile < tiles; tile += gridDim.x) {
+        const size_t next = tile + gridDim.x;
+        if (next < tiles) {
+            double *dst = raw + (stage ^ 1) * 2 * G::RAW;
+            stage_raw<N, TS, AL>(dst, X, next * TS, batch);
+            stage_raw<N, TS, AL>(dst + G::RAW, T, next * TS, batch);
+        }
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        const double *rx = raw + stage * 2 * G::RAW;
+        gather<D, S>(Xp, rx, gb, gs);
+        gather<D, S>(Tp, rx + G::RAW, gb, gs);
+        __syncthreads();
+
+        for (int blk = warp; blk < G::BLOCKS; blk += kWarps) {
+            const double *xb = Xp + blk * 16 * LD;
+            double *tb = Tp + blk * 16 * LD;
+            // GEMM 1: Y'(16 x D) = X'(16 x D) W'(D x D)
+            double acc[G::NT][4];
+#pragma unroll
+            for (int nt = 0; nt < G::NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0;
+#pragma unroll
+            for (int kt = 0; kt < G::KT; ++kt) {
+                const double a0 = xb[g * LD + kt * 4 + t4];
+                const double a1 = xb[(g + 8) * LD + kt * 4 + t4];
+#pragma unroll
+                for (int nt = 0; nt < G::NT; ++nt) mma_16x8x4(acc[nt], a0, a1, bw[kt][nt]);
+            }
+            // Epilogue: R' = Y' - T' in place over T'; loss and finiteness probes.
+#pragma unroll
+            for (int nt = 0; nt < G::NT; ++nt) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    double2 *p = reinterpret_cast<double2 *>(&tb[(g + 8 * h) * LD + nt * 8 + 2 * t4]);
+                    const double2 tv = *p;
+                    double2 r;
+                    r.x = acc[nt][2 * h] - tv.x;
+                    r.y = acc[nt][2 * h + 1] - tv.y;
+                    *p = r;
+                    sq = fma(r.x, r.x, sq);
+                    sq = fma(r.y, r.y, sq);
+                    check_y = fma(acc[nt][2 * h], 0.0, check_y);
+                    check_y = fma(acc[nt][2 * h + 1], 0.0, check_y);
+                    check_r = fma(r.x, 0.0, check_r);
+                    check_r = fma(r.y, 0.0, check_r);
+                }
+            }
+            __syncwarp();
+            // GEMM 2: G'(D x D) += X'^T(D x 16) R'(16 x D); k runs over the 16 rows of the block.
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const int row = kk * 4 + t4;
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    const double a0 = xb[row * LD + m * 16 + g];
+                    const double a1 = (D >= 16) ? xb[row * LD + m * 16 + g + 8] : 0.0;
+#pragma unroll
+                    for (int nt = 0; nt < G::NT; ++nt) {
+                        const double b0 = tb[row * LD + nt * 8 + g];
+                        mma_16x8x4(gacc[m][nt], a0, a1, b0);
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        stage ^= 1;
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // Reduce the warps' G' partials in warp order (deterministic) in shared memory.
+    // Buffers are free now: raw (>= 4*24*32 doubles) holds the kWarps x D x D
+    // partials, X' the summed D x D, T' the 3 x kThreads scalar partials.
+    static_assert(4 * G::RAW >= kWarps * D * D && G::ROWS * LD >= D * D && G::ROWS * LD >= 3 * kThreads,
+                  "epilogue scratch fits");
+    double *Gs = raw;
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+        for (int nt = 0; nt < G::NT; ++nt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int row = m * 16 + g + 8 * h;
+                if (row < D) {
+                    Gs[(warp * D + row) * D + nt * 8 + 2 * t4] = gacc[m][nt][2 * h];
+                    Gs[(warp * D + row) * D + nt * 8 + 2 * t4 + 1] = gacc[m][nt][2 * h + 1];
+                }
+            }
+    double *red = Tp;  // 3 * kThreads doubles
+    red[threadIdx.x] = sq;
+    red[kThreads + threadIdx.x] = check_y;
+    red[2 * kThreads + threadIdx.x] = check_r;
+    __syncthreads();
+    double *Gsum = Xp;  // D * D
+    for (int idx = threadIdx.x; idx < D * D; idx += kThreads) {
+        double acc = 0.0;
+        for (int w = 0; w < kWarps; ++w) acc += Gs[w * D * D + idx];
+        Gsum[idx] = acc;
+    }
+    for (int width = kThreads / 2; width > 0; width >>= 1) {
+        __syncthreads();
+        if (threadIdx.x < width) {
+            red[threadIdx.x] += red[threadIdx.x + width];
+            red[kThreads + threadIdx.x] += red[kThreads + threadIdx.x + width];
+            red[2 * kThreads + threadIdx.x] += red[2 * kThreads + threadIdx.x + width];
+        }
+    }
+    __syncthreads();
+    double *rec = records + (size_t)blockIdx.x * kRecStride;
+    const double inv_s = 1.0 / (double)S;  // exact: S is a power of two
+    if (threadIdx.x < N) {
+        // g_A = <G', rho(e_A)> / S (right) or <G', rho(e_A)^T> / S (left)
+        const int A = threadIdx.x;
+        const int xa = rep.xm[A], za = rep.zm[A];
+        double acc = 0.0;
+        for (int j = 0; j < D; ++j) {
+            // right: entry (j ^ xa, j) with sign (-1)^{za . j}; left: entry (j, j ^ xa), same sign
+            const double v = rep.side ? Gsum[j * D + (j ^ xa)] : Gsum[(j ^ xa) * D + j];
+            acc += (__popc(za & j) & 1) ? -v : v;
+        }
+        rec[A] = (rep.sg[A] < 0 ? -acc : acc) * inv_s;
+    }
+    if (threadIdx.x == 0) {
+        rec[kRecLoss] = 0.5 * red[0] * inv_s;
+        rec[kRecCheckY] = red[kThreads];
+        rec[kRecCheckR] = red[2 * kThreads];
+        rec[kRecCheckIn] = 0.0;
+    }
+}
+
+template <int D, int S, bool AL>
+cudaError_t launch_rep_impl(const RepDevice &rep, const double *X, const double *T, const double *W, size_t batch,
+                            double *records, int *ctas_used, cudaStream_t stream) {
+    using G = RepGeo<D, S>;
+    auto kernel = rep_cycle_kernel<D, S, AL>;
+    const size_t smem = (size_t)(D * D + 2 * G::ROWS * G::LD + 4 * G::RAW) * sizeof(double);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    const size_t tiles = (batch + G::TS - 1) / G::TS;
+    size_t grid = (size_t)device_sm_count() * (size_t)per_sm;
+    if (grid > (size_t)kMaxCtas) grid = kMaxCtas;
+    if (grid > tiles) grid = tiles;
+    if (grid < 1) grid = 1;
+    kernel<<<(unsigned)grid, kThreads, smem, stream>>>(rep, X, T, W, batch, records);
+    if (ctas_used) *ctas_used = (int)grid;
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool rep_supported(const RepDevice &rep) {
+    return (rep.D == 16 && rep.S == 4) || (rep.D == 8 && rep.S == 8) || (rep.D == 8 && rep.S == 4) ||
+           (rep.D == 16 && rep.S == 2);
+}
+
+cudaError_t launch_rep_cycle(const RepDevice &rep, const double *X, const double *T, const double *W, size_t batch,
+                             double *records, int *ctas_used, cudaStream_t stream) {
+    const bool al = (((uintptr_t)X | (uintptr_t)T) & 15u) == 0u;
+#define GEO_REP_CASE(DD, SS)                                                                             \
+    if (rep.D == DD && rep.S == SS)                                                                      \
+        return al ? launch_rep_impl<DD, SS, true>(rep, X, T, W, batch, records, ctas_used, stream)      \
+                  : launch_rep_impl<DD, SS, false>(rep, X, T, W, batch, records, ctas_used, stream);
+    GEO_REP_CASE(16, 4)
+    GEO_REP_CASE(8, 8)
+    GEO_REP_CASE(8, 4)
+    GEO_REP_CASE(16, 2)
+#undef GEO_REP_CASE
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace geo

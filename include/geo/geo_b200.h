@@ -124,6 +124,24 @@ geo_b200_status_t geo_b200_trainer_set_parameter(geo_b200_trainer_t *trainer, co
 geo_b200_status_t geo_b200_trainer_set_state(geo_b200_trainer_t *trainer, const double *parameter,
                                              const double *first_moment, const double *second_moment,
                                              uint64_t step_count);
+/* Kernel family used by the trainer's streaming pass.
+ *  CAYLEY: the 2^n x 2^n sign-folded Cayley matrix on FP64 FMA units (any n).
+ *  REPRESENTATION: a D x D real matrix representation of Cl(p,q) (D = 8 or 16
+ *    for n = 5, 6) on FP64 tensor cores; S*D*D instead of 4^n multiply-adds.
+ *  AUTO (default): REPRESENTATION where available for n >= 5, else CAYLEY.
+ * Both are parity-checked against the reference to 1e-12. */
+typedef enum {
+    GEO_B200_ALGORITHM_AUTO = 0,
+    GEO_B200_ALGORITHM_CAYLEY = 1,
+    GEO_B200_ALGORITHM_REPRESENTATION = 2
+} geo_b200_algorithm_t;
+
+/* Selects the kernel family; INVALID_ARGUMENT when REPRESENTATION is not
+ * available for this algebra and side. */
+geo_b200_status_t geo_b200_trainer_set_algorithm(geo_b200_trainer_t *trainer, geo_b200_algorithm_t algorithm);
+/* The family the next step will use (never AUTO). */
+geo_b200_algorithm_t geo_b200_trainer_algorithm(const geo_b200_trainer_t *trainer);
+
 /* Device pointer to the resident parameter (2^n doubles). */
 const double *geo_b200_trainer_device_parameter(const geo_b200_trainer_t *trainer);
 

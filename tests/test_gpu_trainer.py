@@ -17,8 +17,11 @@ from tests.gpu_helpers import TOL, dev, host, np_ptr, ptr, stream, sync
 pytestmark = pytest.mark.gpu
 
 
+CAYLEY, REPRESENTATION = 1, 2
+
+
 class Trainer:
-    def __init__(self, sig, left, w0, optimizer, lr, b1=0.9, b2=0.999, eps=1e-8):
+    def __init__(self, sig, left, w0, optimizer, lr, b1=0.9, b2=0.999, eps=1e-8, algorithm=0):
         self.L = abi.lib()
         self.h = ctypes.c_void_p()
         cfg = abi.OptimizerConfig(optimizer, lr, b1, b2, eps)
@@ -27,6 +30,8 @@ class Trainer:
                                             np_ptr(w0), ctypes.byref(cfg))
         assert st == 0, st
         self.n = 1 << len(sig)
+        if algorithm:
+            assert self.L.geo_b200_trainer_set_algorithm(self.h, algorithm) == 0
 
     def step(self, dx, dt, batch, scale):
         return self.L.geo_b200_trainer_step_device(self.h, ptr(dx), ptr(dt), batch, scale, stream())
@@ -92,9 +97,10 @@ def test_trainer_sgd_cfg2_cl30(oracle):
     assert tol_close(loss, losses[-1], TOL)
 
 
+@pytest.mark.parametrize("algorithm", [CAYLEY, REPRESENTATION])
 @pytest.mark.parametrize("left,B,steps", [(True, 65536, 6), (False, 65536, 4), (True, 4096, 100),
                                           (False, 4096, 100)])
-def test_trainer_adam_cfg3_cl41(oracle, left, B, steps):
+def test_trainer_adam_cfg3_cl41(oracle, left, B, steps, algorithm):
     """Cl(4,1) Adam lr 1e-3, 0.9/0.999 on both sides: the batch-65536 shape for a
     few steps and the full 100-step schedule at batch 4096 (oracle cost bound)."""
     sig = canonical_signature(5, 1)
@@ -102,7 +108,8 @@ def test_trainer_adam_cfg3_cl41(oracle, left, B, steps):
     x = splitmix_uniform(31 + left, (B, N))
     t = _targets(oracle, sig, left, x, 32 + left)
     w0 = normal(33, (N,), 0.1)
-    tr = Trainer(sig, left, w0, 2, 1e-3)
+    tr = Trainer(sig, left, w0, 2, 1e-3, algorithm=algorithm)
+    assert tr.L.geo_b200_trainer_algorithm(tr.h) == algorithm
     dx, dt = dev(x), dev(t)
     for _ in range(steps):
         assert tr.step(dx, dt, B, 1.0 / B) == 0
@@ -116,7 +123,8 @@ def test_trainer_adam_cfg3_cl41(oracle, left, B, steps):
     assert tol_close(loss, losses[-1], TOL)
 
 
-def test_trainer_matches_golden_v8():
+@pytest.mark.parametrize("algorithm", [0, CAYLEY])
+def test_trainer_matches_golden_v8(algorithm):
     """Golden vectors of the reference's per-sample V8 loop (SGD and Adam, both sides)."""
     import pathlib
 
@@ -127,7 +135,7 @@ def test_trainer_matches_golden_v8():
         dx, dt = dev(xs), dev(ts)
         for opt in (1, 2):
             for side, left in (("R", False), ("L", True)):
-                tr = Trainer(sig, left, w0, opt, 1e-2)
+                tr = Trainer(sig, left, w0, opt, 1e-2, algorithm=algorithm)
                 want = golden[f"v8_n{n}q{q}{side}_opt{opt}_w"]
                 losses = golden[f"v8_n{n}q{q}{side}_opt{opt}_loss"]
                 for k in range(3):
@@ -182,3 +190,58 @@ def test_trainer_transactional_failure():
     assert all(np.array_equal(u, v) for u, v in zip(before[:3], after[:3])) and after[3] == before[3]
     assert tr.step(dx, dt, 64, 1 / 64) == 0
     assert tr.sync()[0] == 0 and tr.state()[3] == before[3] + 1
+
+
+@pytest.mark.parametrize("n", [5, 6])
+def test_representation_all_signatures(oracle, n):
+    """The tensor-core representation path on every Cl(p,q) with p+q = n, both sides:
+    three Adam steps on 3000 samples (ragged last tile) against the oracle."""
+    from tests.conftest import all_signatures
+
+    N = 1 << n
+    B = 3000
+    for _, q, sig in all_signatures(n, n):
+        for left in (False, True):
+            x = splitmix_uniform(700 + 10 * q + left, (B, N))
+            t = _targets(oracle, sig, left, x, 800 + q)
+            w0 = normal(900 + q, (N,), 0.125)
+            tr = Trainer(sig, left, w0, 2, 1e-3, algorithm=REPRESENTATION)
+            dx, dt = dev(x), dev(t)
+            losses = []
+            for _ in range(3):
+                assert tr.step(dx, dt, B, 1.0 / B) == 0
+                st, loss = tr.sync()
+                assert st == 0
+                losses.append(loss)
+            w, m, v, count = tr.state()
+            w_ref, m_ref, v_ref, l_ref = _oracle_train(oracle, sig, left, x, t, w0, 2, 1e-3, 3)
+            assert count == 3
+            assert tol_close(w, w_ref, TOL), (n, q, left, max_violation(w, w_ref, TOL))
+            assert tol_close(m, m_ref, TOL) and tol_close(v, v_ref, TOL)
+            assert tol_close(losses, l_ref, TOL), (losses, l_ref)
+
+
+@pytest.mark.parametrize("q", [0, 3])
+def test_representation_matches_cayley_full_size(q):
+    """At the full 2^22-sample Cl(6,0) / Cl(3,3) shape the two independent kernel
+    families give the same gradient record: one Adam step from the same state
+    lands on the same parameters and loss (1e-12)."""
+    import torch
+
+    sig = canonical_signature(6, q)
+    B = 1 << 22
+    gen = torch.Generator(device="cuda").manual_seed(40 + q)
+    X = torch.rand((B, 64), dtype=torch.float64, device="cuda", generator=gen) * 2 - 1
+    T = torch.rand((B, 64), dtype=torch.float64, device="cuda", generator=gen) * 2 - 1
+    w0 = normal(41 + q, (64,), 0.125)
+    results = []
+    for algorithm in (CAYLEY, REPRESENTATION):
+        tr = Trainer(sig, False, w0, 2, 1e-3, algorithm=algorithm)
+        assert tr.step(X, T, B, 1.0 / B) == 0
+        st, loss = tr.sync()
+        assert st == 0
+        results.append((tr.state(), loss))
+    (s1, l1), (s2, l2) = results
+    assert tol_close(l1, l2, TOL)
+    for a, b in zip(s1[:3], s2[:3]):
+        assert tol_close(a, b, TOL), max_violation(a, b, TOL)
