@@ -132,9 +132,17 @@ struct RepDevice {
     uint8_t xm[64];
     uint8_t zm[64];
     int8_t sg[64];
-    uint8_t gb[8][64];   // [term][kept entry] blade
-    int8_t gs[8][64];    // [term][kept entry] sign
+    // Gather by blade group: the thread of group m (blades with x-mask m, c of
+    // them) loads grp_blade[m][t] at step t and writes kept row r, column
+    // grp_col[m][r], with input t negated when bit (r * 8 + t) of grp_neg[m] is
+    // set. The load order is an edge colouring of (lane, bank) so each load
+    // instruction of a warp touches distinct shared-memory banks.
+    uint8_t grp_blade[16][8];
+    uint8_t grp_col[16][8];
+    uint64_t grp_neg[16];
     int32_t blades, D, S, side;
+    int32_t raw_stride;  // padded row stride (doubles) of the staged raw tiles
+    int32_t reserved;
 };
 bool make_rep_device(RepDevice *out, const RepPlan &plan);
 // True when a tensor-core kernel exists for the plan's (D, S).

@@ -222,9 +222,15 @@ tiled_kernel(const SignPlan plan, const double *__restrict__ in, const double *_
                 for (int q = 0; q < QC; ++q) {
                     const int o = 2 * og + 2 * OG * q;
                     if (MODE == kModeForward) {
-                        if (sample < batch)
-                            *reinterpret_cast<double2 *>(&out[sample * N + o]) =
-                                make_double2(acc[j][q][0], acc[j][q][1]);
+                        if (sample < batch) {
+                            if (ALIGNED16) {
+                                *reinterpret_cast<double2 *>(&out[sample * N + o]) =
+                                    make_double2(acc[j][q][0], acc[j][q][1]);
+                            } else {  // 8-byte aligned output: scalar stores only
+                                out[sample * N + o] = acc[j][q][0];
+                                out[sample * N + o + 1] = acc[j][q][1];
+                            }
+                        }
                     } else {
                         const double2 t = *reinterpret_cast<const double2 *>(&Ts[s * LD + o]);
                         double2 r;
@@ -238,8 +244,14 @@ tiled_kernel(const SignPlan plan, const double *__restrict__ in, const double *_
                         check_y = fma(acc[j][q][1], 0.0, check_y);
                         check_r = fma(r.x, 0.0, check_r);
                         check_r = fma(r.y, 0.0, check_r);
-                        if (out != nullptr && sample < batch)
-                            *reinterpret_cast<double2 *>(&out[sample * N + o]) = r;
+                        if (out != nullptr && sample < batch) {
+                            if (ALIGNED16) {
+                                *reinterpret_cast<double2 *>(&out[sample * N + o]) = r;
+                            } else {
+                                out[sample * N + o] = r.x;
+                                out[sample * N + o + 1] = r.y;
+                            }
+                        }
                     }
                 }
             }

@@ -29,25 +29,6 @@
 
 namespace geo {
 
-bool make_rep_device(RepDevice *out, const RepPlan &p) {
-    if (!p.valid) return false;
-    for (int A = 0; A < 64; ++A) {
-        out->xm[A] = p.xm[A];
-        out->zm[A] = p.zm[A];
-        out->sg[A] = p.sg[A];
-    }
-    for (int t = 0; t < 8; ++t)
-        for (int e = 0; e < 64; ++e) {
-            out->gb[t][e] = t < p.c ? p.gb[e][t] : 0;
-            out->gs[t][e] = t < p.c ? p.gs[e][t] : 0;
-        }
-    out->blades = p.blades;
-    out->D = p.D;
-    out->S = p.S;
-    out->side = p.side;
-    return true;
-}
-
 namespace {
 
 constexpr int kThreads = 256;
@@ -87,48 +68,53 @@ struct RepGeo {
     static constexpr int BLOCKS = ROWS / 16;
     static constexpr int NT = D / 8;        // 8-column tiles of the D outputs
     static constexpr int KT = D / 4;        // k-steps of GEMM 1
-    static constexpr int RAW = TS * N;      // doubles of one raw tile
+    static constexpr int RAW = TS * (N + 8);  // doubles of one raw tile (padded rows)
     static_assert(ROWS % 16 == 0 && D % 8 == 0, "tile shape");
 };
 
 template <int N, int TS, bool AL>
-__device__ __forceinline__ void stage_raw(double *dst, const double *__restrict__ src, size_t first, size_t batch) {
+__device__ __forceinline__ void stage_raw(double *dst, const double *__restrict__ src, size_t first, size_t batch,
+                                          int rs) {
     if (AL) {
         for (int c = threadIdx.x; c < TS * (N / 2); c += kThreads) {
             const int s = c / (N / 2);
+            const int k2 = c - s * (N / 2);
             const size_t sample = first + (size_t)s;
             const bool ok = sample < batch;
-            const double *g = ok ? src + first * N + 2 * (size_t)c : src;
-            cp_async_16(dst + 2 * c, g, ok ? 16 : 0);
+            const double *g = ok ? src + sample * N + 2 * k2 : src;
+            cp_async_16(dst + s * rs + 2 * k2, g, ok ? 16 : 0);
         }
     } else {
         for (int c = threadIdx.x; c < TS * N; c += kThreads) {
             const int s = c / N;
+            const int k = c - s * N;
             const size_t sample = first + (size_t)s;
             const bool ok = sample < batch;
-            const double *g = ok ? src + first * N + (size_t)c : src;
-            cp_async_8(dst + c, g, ok ? 8 : 0);
+            const double *g = ok ? src + sample * N + k : src;
+            cp_async_8(dst + s * rs + k, g, ok ? 8 : 0);
         }
     }
 }
 
-// X'[(s*S + r) * LD + k] = sum_t gs[t][e] raw[s*N + gb[t][e]],  e = r*D + k.
+// Signed gather by blade group: the thread of group m loads each of its S
+// blades once and writes the S kept entries (s*S + r, grp_col[m][r]).
 template <int D, int S>
-__device__ __forceinline__ void gather(double *dst, const double *raw, const uint8_t *gb, const int8_t *gs) {
+__device__ __forceinline__ void gather(double *dst, const double *raw, int rs, int m, int slice,
+                                       const int (&blade)[S], const int (&col)[S], uint64_t neg) {
     using G = RepGeo<D, S>;
-    for (int idx = threadIdx.x; idx < G::TS * G::N; idx += kThreads) {
-        const int s = idx / G::N;
-        const int e = idx - s * G::N;
-        const double *row = raw + s * G::N;
-        double acc = 0.0;
+    constexpr int SLICES = kThreads / D;
+    for (int s = slice; s < G::TS; s += SLICES) {
+        const double *row = raw + s * rs;
+        double in[S];
 #pragma unroll
-        for (int t = 0; t < S; ++t) {
-            const double v = row[gb[t * 64 + e]];
-            acc = gs[t * 64 + e] > 0 ? acc + v : acc - v;
+        for (int t = 0; t < S; ++t) in[t] = row[blade[t]];
+#pragma unroll
+        for (int r = 0; r < S; ++r) {
+            double acc = 0.0;
+#pragma unroll
+            for (int t = 0; t < S; ++t) acc = ((neg >> (r * 8 + t)) & 1ull) ? acc - in[t] : acc + in[t];
+            dst[(s * S + r) * G::LD + col[r]] = acc;
         }
-        const int r = e / D;
-        const int k = e - r * D;
-        dst[(s * S + r) * G::LD + k] = acc;
     }
 }
 
@@ -142,17 +128,23 @@ rep_cycle_kernel(const RepDevice rep, const double *__restrict__ X, const double
     double *Wp = smem;                              // D*D
     double *Xp = Wp + D * D;                        // ROWS*LD
     double *Tp = Xp + G::ROWS * LD;                 // ROWS*LD (T', then R')
-    double *raw = Tp + G::ROWS * LD;                // 2 stages x (x tile, t tile)
-    __shared__ uint8_t gb[8 * 64];
-    __shared__ int8_t gs[8 * 64];
+    double *raw = Tp + G::ROWS * LD;                // 2 stages x (x tile, t tile), padded rows
+    const int rs = rep.raw_stride;
+    const int raw_tile = TS * rs;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t4 = lane & 3;
 
-    for (int i = threadIdx.x; i < 8 * 64; i += kThreads) {
-        gb[i] = rep.gb[i / 64][i % 64];
-        gs[i] = rep.gs[i / 64][i % 64];
+    // This thread's blade group for the gathers, resident for the whole kernel.
+    const int gm = threadIdx.x % D;
+    const int gslice = threadIdx.x / D;
+    int gblade[S], gcol[S];
+#pragma unroll
+    for (int t = 0; t < S; ++t) {
+        gblade[t] = rep.grp_blade[gm][t];
+        gcol[t] = rep.grp_col[gm][t];
     }
+    const uint64_t gneg = rep.grp_neg[gm];
     // W' = rho(W) (right) or rho(W)^T (left): W'[k][j] = sum_{A: x_A = k^j} W_A sg_A (-1)^{z_A . col}
     for (int idx = threadIdx.x; idx < D * D; idx += kThreads) {
         const int k = idx / D, j = idx - k * D;
@@ -170,8 +162,8 @@ rep_cycle_kernel(const RepDevice rep, const double *__restrict__ X, const double
     const size_t tiles = (batch + TS - 1) / TS;
     size_t tile = blockIdx.x;
     if (tile < tiles) {
-        stage_raw<N, TS, AL>(raw, X, tile * TS, batch);
-        stage_raw<N, TS, AL>(raw + G::RAW, T, tile * TS, batch);
+        stage_raw<N, TS, AL>(raw, X, tile * TS, batch, rs);
+        stage_raw<N, TS, AL>(raw + raw_tile, T, tile * TS, batch, rs);
     }
     cp_async_commit();
     __syncthreads();
@@ -196,16 +188,16 @@ rep_cycle_kernel(const RepDevice rep, const double *__restrict__ X, const double
     for (; tile < tiles; tile += gridDim.x) {
         const size_t next = tile + gridDim.x;
         if (next < tiles) {
-            double *dst = raw + (stage ^ 1) * 2 * G::RAW;
-            stage_raw<N, TS, AL>(dst, X, next * TS, batch);
-            stage_raw<N, TS, AL>(dst + G::RAW, T, next * TS, batch);
+            double *dst = raw + (stage ^ 1) * 2 * raw_tile;
+            stage_raw<N, TS, AL>(dst, X, next * TS, batch, rs);
+            stage_raw<N, TS, AL>(dst + raw_tile, T, next * TS, batch, rs);
         }
         cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
-        const double *rx = raw + stage * 2 * G::RAW;
-        gather<D, S>(Xp, rx, gb, gs);
-        gather<D, S>(Tp, rx + G::RAW, gb, gs);
+        const double *rx = raw + stage * 2 * raw_tile;
+        gather<D, S>(Xp, rx, rs, gm, gslice, gblade, gcol, gneg);
+        gather<D, S>(Tp, rx + raw_tile, rs, gm, gslice, gblade, gcol, gneg);
         __syncthreads();
 
         for (int blk = warp; blk < G::BLOCKS; blk += kWarps) {
@@ -267,7 +259,7 @@ rep_cycle_kernel(const RepDevice rep, const double *__restrict__ X, const double
     // Reduce the warps' G' partials in warp order (deterministic) in shared memory.
     // Buffers are free now: raw (>= 4*24*32 doubles) holds the kWarps x D x D
     // partials, X' the summed D x D, T' the 3 x kThreads scalar partials.
-    static_assert(4 * G::RAW >= kWarps * D * D && G::ROWS * LD >= D * D && G::ROWS * LD >= 3 * kThreads,
+    static_assert(4 * G::TS * N >= kWarps * D * D && G::ROWS * LD >= D * D && G::ROWS * LD >= 3 * kThreads,
                   "epilogue scratch fits");
     double *Gs = raw;
 #pragma unroll
@@ -328,6 +320,7 @@ template <int D, int S, bool AL>
 cudaError_t launch_rep_impl(const RepDevice &rep, const double *X, const double *T, const double *W, size_t batch,
                             double *records, int *ctas_used, cudaStream_t stream) {
     using G = RepGeo<D, S>;
+    if (rep.raw_stride != G::N + 8 || rep.D != D || rep.S != S) return cudaErrorInvalidValue;
     auto kernel = rep_cycle_kernel<D, S, AL>;
     const size_t smem = (size_t)(D * D + 2 * G::ROWS * G::LD + 4 * G::RAW) * sizeof(double);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

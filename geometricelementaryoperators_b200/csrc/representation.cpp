@@ -3,6 +3,7 @@
 #include "representation.h"
 
 #include <cstring>
+#include <utility>
 #include <vector>
 
 #include "geo_internal.h"
@@ -181,6 +182,91 @@ bool make_rep_plan(RepPlan *out, uint8_t dimension, const int8_t *signature, int
     }
     std::memset(out, 0, sizeof(*out));
     return false;
+}
+
+namespace {
+
+// Perfect matching on a bipartite graph (left = lanes, right = bank classes)
+// by augmenting paths; adj[l] lists candidate edges as (class, edge id).
+bool augment(int l, const std::vector<std::vector<std::pair<int, int>>> &adj, std::vector<int> &match_r,
+             std::vector<int> &edge_of_r, std::vector<char> &seen) {
+    for (const auto &ce : adj[l]) {
+        const int r = ce.first;
+        if (seen[r]) continue;
+        seen[r] = 1;
+        if (match_r[r] < 0 || augment(match_r[r], adj, match_r, edge_of_r, seen)) {
+            match_r[r] = l;
+            edge_of_r[r] = ce.second;
+            return true;
+        }
+    }
+    return false;
+}
+
+}  // namespace
+
+bool make_rep_device(RepDevice *out, const RepPlan &p) {
+    if (!p.valid || p.S > 8 || p.D > 16) return false;
+    std::memset(out, 0, sizeof(*out));
+    for (int A = 0; A < 64; ++A) {
+        out->xm[A] = p.xm[A];
+        out->zm[A] = p.zm[A];
+        out->sg[A] = p.sg[A];
+    }
+    const int D = p.D, S = p.S, N = p.blades, c = p.c;
+    out->blades = N;
+    out->D = D;
+    out->S = S;
+    out->side = p.side;
+    // Bank classes: with 32 / D samples per warp instruction, rows padded so
+    // consecutive samples shift by 8 double-banks; a lane's load must then be
+    // distinct modulo `mod` among the D lanes of one sample.
+    const int mod = D >= 16 ? 16 : 8;
+    out->raw_stride = N + 8;
+    // Group members and their signs from the kept-entry gather table.
+    std::vector<std::vector<int>> members(D);
+    for (int A = 0; A < N; ++A) members[p.xm[A]].push_back(A);
+    for (int m = 0; m < D; ++m)
+        if ((int)members[m].size() != c) return false;
+    // Edge-colour the c-regular bipartite multigraph (group m) x (blade mod `mod`)
+    // into c perfect matchings: matching t gives every group its load at step t.
+    std::vector<std::vector<int>> remaining = members;
+    for (int t = 0; t < c; ++t) {
+        std::vector<std::vector<std::pair<int, int>>> adj(D);
+        for (int m = 0; m < D; ++m)
+            for (int i = 0; i < (int)remaining[m].size(); ++i) adj[m].push_back({remaining[m][i] % mod, i});
+        std::vector<int> match_r(mod, -1), edge_of_r(mod, -1);
+        for (int m = 0; m < D; ++m) {
+            std::vector<char> seen(mod, 0);
+            if (!augment(m, adj, match_r, edge_of_r, seen)) return false;
+        }
+        std::vector<int> take(D, -1);
+        for (int r = 0; r < mod; ++r)
+            if (match_r[r] >= 0) take[match_r[r]] = edge_of_r[r];
+        for (int m = 0; m < D; ++m) {
+            if (take[m] < 0) return false;
+            out->grp_blade[m][t] = (uint8_t)remaining[m][take[m]];
+            remaining[m].erase(remaining[m].begin() + take[m]);
+        }
+    }
+    for (int m = 0; m < D; ++m) {
+        uint64_t neg = 0;
+        for (int r = 0; r < S; ++r) {
+            const int k = p.rows[r] ^ m;
+            out->grp_col[m][r] = (uint8_t)k;
+            const int e = r * D + k;
+            for (int t = 0; t < c; ++t) {
+                const int A = out->grp_blade[m][t];
+                int sign = 0;
+                for (int u = 0; u < c; ++u)
+                    if (p.gb[e][u] == A) sign = p.gs[e][u];
+                if (sign == 0) return false;
+                if (sign < 0) neg |= (uint64_t)1 << (r * 8 + t);
+            }
+        }
+        out->grp_neg[m] = neg;
+    }
+    return true;
 }
 
 }  // namespace geo

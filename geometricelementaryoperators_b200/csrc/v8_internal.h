@@ -1,0 +1,51 @@
+// v8_internal.h -- shared pieces of the V8 graph runtime (v8_host.cpp, v8_kernels.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "geo/full_cycle_v8.h"
+
+namespace geo {
+namespace v8 {
+
+// The node array of a program is one mapped, page-locked host allocation:
+//   [ node_capacity x geo_v8_node_t | node_capacity x Candidate | Control ]
+// Callers see only `nodes`; the trailing area holds the optimizer's
+// transactional candidates and the device-written status word.
+struct Candidate {
+    double value[64];
+    double first[64];
+    double second[64];
+};
+
+struct Control {
+    int32_t status;      // geo_v8_status_t written by the kernels
+    int32_t failed_node; // first node that failed (diagnostics)
+    int32_t pad[14];
+};
+
+size_t allocation_bytes(size_t capacity);
+Candidate *candidates(geo_v8_node_t *nodes, size_t capacity);
+Control *control(geo_v8_node_t *nodes, size_t capacity);
+
+// Validation helpers with the reference's rules (src/full_cycle_v8.c:7-130).
+bool dimension_valid(unsigned n);
+bool signature_valid(const int8_t *signature, unsigned n);
+bool mv_valid(const geo_operator_mv_f64_t *value, unsigned n, const int8_t *signature);
+bool program_valid(const geo_v8_program_t *program);
+bool node_exists(const geo_v8_program_t *program, geo_v8_node_id_t id);
+bool leaf_kind(int kind);
+bool unary_kind(int kind);
+bool binary_kind(int kind);
+void mv_zero(geo_operator_mv_f64_t *value, unsigned n, const int8_t *signature);
+
+// Device execution (v8_kernels.cu); each call launches and waits.
+geo_v8_status_t run_forward(geo_v8_program_t *program);
+geo_v8_status_t run_backward(geo_v8_program_t *program, int accumulate);
+geo_v8_status_t run_optimizer(geo_v8_program_t *program, int optimizer, double learning_rate, double beta1,
+                              double beta2, double epsilon, double gradient_scale, double bias1, double bias2);
+
+}  // namespace v8
+}  // namespace geo

@@ -160,6 +160,27 @@ void geo_b200_comm_destroy(geo_b200_comm_t *comm);
 void geo_b200_comm_abort(geo_b200_comm_t *comm);
 geo_b200_status_t geo_b200_trainer_attach_comm(geo_b200_trainer_t *trainer, geo_b200_comm_t *comm);
 
+/* ---- 2b. batched V8 programs ------------------------------------------ */
+
+/* One optimizer step of a compiled V8 program over a device-resident
+ * minibatch, equal to: geo_v8_zero_grad; for every sample s: set the INPUT
+ * node to inputs[s] and the TARGET node to targets[s], geo_v8_forward,
+ * geo_v8_backward(accumulate = s != 0); then geo_v8_optimizer_step(optimizer,
+ * ..., gradient_scale). The program must be the graph
+ *   gp = GEOMETRIC_PRODUCT(input, w) or (w, input);  neg = SCALE(target, -1);
+ *   residual = ADD(gp, neg) (either order);  loss = SQUARED_NORM(residual)
+ * with `w` its only PARAMETER (no constraint) and `loss` its loss node;
+ * anything else returns GEO_V8_BAD_PROGRAM. The parameter's value and Adam
+ * moments are updated in place in the program (transactional), the step
+ * count advances, gradients are cleared, and the INPUT/TARGET node values are
+ * left unchanged. *loss_sum (may be NULL) receives sum_s 0.5 |r_s|^2.
+ * Synchronous; returns geo_v8_status_t values (declared in
+ * geo/full_cycle_v8.h, passed here as int to keep this header independent). */
+int geo_b200_v8_batch_train_step(void *program, uint32_t input_node, uint32_t target_node,
+                                 const double *device_inputs, const double *device_targets, size_t batch,
+                                 int optimizer, double learning_rate, double beta1, double beta2, double epsilon,
+                                 double gradient_scale, double *loss_sum);
+
 /* ---- 3. pairwise products (both operands vary per element) ------------ */
 
 /* out[s] = left[s] * right[s]. */

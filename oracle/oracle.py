@@ -317,6 +317,22 @@ class Reference:
         return self._coeffs(ic, len(signature)), pc
 
     # -- V8 graph runtime (reference src/full_cycle_v8.c) --------------------
+    def v8_composed(self, signature, values) -> tuple[float, np.ndarray, np.ndarray]:
+        """Forward + backward of the all-node-kinds graph: (loss, grad w1, grad w2)."""
+        L = self.lib
+        n = len(signature)
+        prog = (ctypes.c_uint8 * 256)()
+        ids = composed_graph(L, prog, signature, lambda c: self._mv(signature, c), values)
+        try:
+            assert L.geo_v8_forward(prog) == 0
+            assert L.geo_v8_backward(prog, 0) == 0
+            loss = ctypes.cast(L.geo_v8_value(prog, ids["loss"]), ctypes.POINTER(MvF64)).contents.coefficients[0]
+            g1 = self._coeffs(ctypes.cast(L.geo_v8_gradient(prog, ids["p1"]), ctypes.POINTER(MvF64)).contents, n)
+            g2 = self._coeffs(ctypes.cast(L.geo_v8_gradient(prog, ids["p2"]), ctypes.POINTER(MvF64)).contents, n)
+        finally:
+            L.geo_v8_program_free(prog)
+        return loss, g1, g2
+
     def v8_train(self, signature, left: bool, xs, ts, w0, optimizer: int, lr: float, b1: float, b2: float,
                  eps: float, steps: int):
         """Per-sample V8 loop of the graph x*w (or w*x) -> add(., scale(t,-1)) -> squared_norm.
@@ -362,6 +378,53 @@ class Reference:
         finally:
             L.geo_v8_program_free(prog)
         return np.array(params), np.array(losses)
+
+
+def composed_graph(L, prog, signature, mv, values) -> dict:
+    """Build the all-node-kinds graph of the reference test
+    (tests/test_full_cycle_v8.c:158-181) through any library exposing the
+    geo_v8_* ABI. `mv(coeffs)` builds a geo_operator_mv_f64_t for `signature`;
+    `values` holds the input, target, w1, w2 coefficient arrays. Returns node ids."""
+    n = len(signature)
+    q = sum(1 for s in signature if s < 0)
+    ids = {}
+
+    def nid(name):
+        ids[name] = ctypes.c_uint32()
+        return ctypes.byref(ids[name])
+
+    const = np.zeros(1 << n)
+    const[0] = 1.25
+    assert L.geo_v8_program_init(prog, n, sig_array(signature), 1, 4) == 0
+    assert L.geo_v8_add_leaf(prog, 1, b"x", ctypes.byref(mv(values["input"])), 1, 0, nid("x")) == 0
+    assert L.geo_v8_add_leaf(prog, 2, b"target", ctypes.byref(mv(values["target"])), 0, 0, nid("y")) == 0
+    assert L.geo_v8_add_leaf(prog, 3, b"w1", ctypes.byref(mv(values["w1"])), 1, 0, nid("p1")) == 0
+    assert L.geo_v8_add_leaf(prog, 3, b"w2", ctypes.byref(mv(values["w2"])), 1, 0, nid("p2")) == 0
+    assert L.geo_v8_add_leaf(prog, 4, b"bias", ctypes.byref(mv(const)), 0, 0, nid("c0")) == 0
+    assert L.geo_v8_add_binary(prog, 8, b"gp", ids["x"], ids["p1"], nid("gp")) == 0
+    assert L.geo_v8_add_unary(prog, 14, b"activation", ids["gp"], 0.0, 0, nid("act")) == 0
+    assert L.geo_v8_add_unary(prog, 15, b"gate", ids["p2"], 0.0, 0, nid("gate")) == 0
+    assert L.geo_v8_add_binary(prog, 13, b"gated", ids["act"], ids["gate"], nid("gated")) == 0
+    assert L.geo_v8_add_unary(prog, 9, b"reversed", ids["gated"], 0.0, 0, nid("rev")) == 0
+    assert L.geo_v8_add_unary(prog, 11, b"involuted", ids["rev"], 0.0, 0, nid("inv")) == 0
+    assert L.geo_v8_add_unary(prog, 12, b"conjugated", ids["inv"], 0.0, 0, nid("conj")) == 0
+    assert L.geo_v8_add_unary(prog, 10, b"projected", ids["conj"], 0.0, q % (n + 1), nid("proj")) == 0
+    assert L.geo_v8_add_binary(prog, 6, b"shifted", ids["proj"], ids["c0"], nid("shift")) == 0
+    assert L.geo_v8_add_unary(prog, 16, b"normalized", ids["shift"], 1e-12, 0, nid("norm")) == 0
+    assert L.geo_v8_add_unary(prog, 7, b"negative_target", ids["y"], -1.0, 0, nid("negy")) == 0
+    assert L.geo_v8_add_binary(prog, 6, b"residual", ids["norm"], ids["negy"], nid("res")) == 0
+    assert L.geo_v8_add_unary(prog, 17, b"loss", ids["res"], 0.0, 0, nid("loss")) == 0
+    assert L.geo_v8_compile(prog, ids["loss"]) == 0
+    return ids
+
+
+def v8_mv_fill(n: int, seed: int) -> np.ndarray:
+    """Coefficients of mv_fill in the reference test (tests/test_full_cycle_v8.c:29-41)."""
+    out = np.zeros(1 << n)
+    for blade in range(1 << n):
+        mixed = ((blade + 1) * (seed * 31 + 17) + seed * 7) & 0xFFFFFFFF
+        out[blade] = float(mixed % 29 - 14) / 23.0
+    return out
 
 
 class MvF64(ctypes.Structure):

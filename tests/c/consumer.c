@@ -36,7 +36,8 @@ int main(void) {
         double ls = -1.0;
         CHECK(geo_b200_trainer_create(&tr, 6, sig, 0, w, &cfg) == GEO_B200_OK);
         CHECK(geo_b200_trainer_step_host(tr, x, t, B, 1.0 / B, &ls) == GEO_B200_OK);
-        CHECK(ls == 0.0);
+        /* targets are this library's own forward outputs: the loss is rounding-level */
+        CHECK(ls >= 0.0 && ls < 1e-20 * B);
         geo_b200_trainer_destroy(tr);
     }
     puts("GEO_B200_CONSUMER: PASS");

@@ -64,6 +64,27 @@ int main() {
                 double err = 0;
                 for (int o = 0; o < N; ++o) err = std::fmax(err, std::fabs(y[o] - y_ref[o]));
                 if (err > 1e-12) { printf("FAIL n=%d q=%d side=%d err=%g\n", n, q, side, err); return 1; }
+                RepDevice dev;
+                if (!make_rep_device(&dev, p)) { printf("FAIL device tables n=%d q=%d side=%d\n", n, q, side); return 1; }
+                // Grouped gather == entry gather, and every warp load step hits distinct bank classes.
+                double Xg[64] = {0};
+                for (int m = 0; m < D; ++m)
+                    for (int r = 0; r < S; ++r) {
+                        double acc = 0;
+                        for (int t = 0; t < S; ++t) {
+                            const double v = x[dev.grp_blade[m][t]];
+                            acc += ((dev.grp_neg[m] >> (r * 8 + t)) & 1) ? -v : v;
+                        }
+                        Xg[r * D + dev.grp_col[m][r]] = acc;
+                    }
+                for (int e = 0; e < N; ++e)
+                    if (std::fabs(Xg[e] - Xp[e]) > 1e-12) { printf("FAIL grouped gather n=%d q=%d\n", n, q); return 1; }
+                const int mod = D >= 16 ? 16 : 8;
+                for (int t = 0; t < S; ++t) {
+                    unsigned used = 0;
+                    for (int m = 0; m < D; ++m) used |= 1u << (dev.grp_blade[m][t] % mod);
+                    if (__builtin_popcount(used) != D) { printf("FAIL bank classes n=%d q=%d\n", n, q); return 1; }
+                }
                 printf("n=%d q=%d side=%d D=%d S=%d err=%.1e\n", n, q, side, D, S, err);
                 ++cases;
             }

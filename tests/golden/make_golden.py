@@ -12,7 +12,9 @@ and stores inputs and outputs as exact float64 arrays:
 * dense pairwise GP / VJP / JVP (src/operator_kernel.c:412-539) per signature;
 * sparse plans (src/operator_kernel.c:191-334) with terms {0:+1, 1:-2, top:+1};
 * the V8 per-sample loop (src/full_cycle_v8.c) with SGD and Adam, 3 steps on
-  3 samples, for a handful of signatures and both sides.
+  3 samples, for a handful of signatures and both sides;
+* the all-node-kinds V8 graph of the reference test (tests/test_full_cycle_v8.c:
+  158-181): loss and the gradients of both parameters, every signature.
 
 Usage: python tests/golden/make_golden.py
 """
@@ -84,6 +86,14 @@ def main() -> None:
                 params, losses = ref.v8_train(sig, left, xs, ts, w0, opt, 1e-2, 0.9, 0.999, 1e-8, steps=3)
                 data[f"v8_n{n}q{q}{side}_opt{opt}_w"] = params
                 data[f"v8_n{n}q{q}{side}_opt{opt}_loss"] = losses
+    for n in range(1, 7):
+        for q in range(n + 1):
+            sig = canonical_signature(n, q)
+            values = {"input": orc.v8_mv_fill(n, 3 + n + q), "target": orc.v8_mv_fill(n, 11 + 2 * n + q),
+                      "w1": orc.v8_mv_fill(n, 19 + n + q), "w2": orc.v8_mv_fill(n, 29 + n + q)}
+            loss, g1, g2 = ref.v8_composed(sig, values)
+            data[f"v8c_n{n}q{q}_loss"] = np.array([loss])
+            data[f"v8c_n{n}q{q}_g1"], data[f"v8c_n{n}q{q}_g2"] = g1, g2
     np.savez_compressed(OUT, **data)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes, {len(data)} arrays)")
 
