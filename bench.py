@@ -45,6 +45,11 @@ def parse():
     p.add_argument("--batch-log2", type=int, default=22, help="per-GPU batch = 2^k (22 is the headline shape)")
     p.add_argument("--negative", type=int, default=0, help="q of Cl(6-q, q); 0 = Cl(6,0)")
     p.add_argument("--no-extras", action="store_true", help="skip e2e, Cl(3,3) and cpu_baseline legs")
+    p.add_argument("--leg", choices=["train", "pairwise-f32"], default="train",
+                   help="pairwise-f32: run only the float32 pairwise sweep (for profiling)")
+    p.add_argument("--pairwise-log2", type=int, default=26, help="batch 2^k of the float32 pairwise sweep")
+    p.add_argument("--algorithm", choices=["auto", "cayley", "representation"], default="auto",
+                   help="kernel family of the headline step (auto picks the representation for n = 6)")
     return p.parse_args()
 
 
@@ -79,7 +84,8 @@ def max_over_ranks(value: float, world: int) -> float:
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -282,6 +288,42 @@ def cpu_baseline_leg(negative: int) -> dict:
             "sample": f"{chunks} chunks of 1024 samples of the Cl(6,{negative}) shape (forward+VJP), {dt:.1f} s"}
 
 
+def pairwise_f32_leg(lib, args, world) -> dict:
+    """y = a * b per element, float32, Cl(6,0); a even-grade stored compact."""
+    import torch
+
+    from geometricelementaryoperators_b200 import abi
+
+    batch = 1 << args.pairwise_log2
+    gen = torch.Generator(device="cuda").manual_seed(77)
+    a = torch.randn((batch, 32), dtype=torch.float32, device="cuda", generator=gen)
+    b = torch.rand((batch, 64), dtype=torch.float32, device="cuda", generator=gen).mul_(2).sub_(1)
+    y = torch.empty((batch, 64), dtype=torch.float32, device="cuda")
+    sig = abi.sig_array([1] * 6)
+    sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    ap, bp, yp = (ctypes.c_void_p(t.data_ptr()) for t in (a, b, y))
+    for _ in range(2):
+        assert lib.geo_b200_pairwise_gp_f32(6, sig, ap, 1, bp, yp, batch, sp) == 0
+    torch.cuda.synchronize()
+    reps = 5
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        assert lib.geo_b200_pairwise_gp_f32(6, sig, ap, 1, bp, yp, batch, sp) == 0
+    e.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e) / reps, world)
+    bytes_per = (32 + 64 + 64) * 4
+    gbs = batch * bytes_per / (ms / 1e3) / 1e9
+    hbm_peak, _ = peaks()
+    del a, b, y
+    torch.cuda.empty_cache()
+    return {"workload": "Cl(6,0) float32 pairwise products, even-grade left (compact 32) x dense right, "
+                        f"batch 2^{args.pairwise_log2} per GPU", "value": batch * world / (ms / 1e3), "unit": "products/s",
+            "ms_per_launch": ms, "bytes_per_product": bytes_per, "achieved_gbs": gbs,
+            "hbm_frac": gbs / hbm_peak, "flops_per_product": 2 * 32 * 64}
+
+
 # --------------------------------------------------------------------------- main arm
 def run_b200(args, world, rank, local):
     import numpy as np
@@ -294,7 +336,7 @@ def run_b200(args, world, rank, local):
     q = args.negative
     sig = [1] * (6 - q) + [-1] * q
     X, T, w0 = make_data(lib, sig, batch, 1234 + rank)
-    tr = Trainer(lib, sig, w0)
+    tr = Trainer(lib, sig, w0, algorithm={"auto": 0, "cayley": 1, "representation": 2}[args.algorithm])
     comm = ctypes.c_void_p()
     if world > 1:
         import torch.distributed as dist
@@ -381,6 +423,9 @@ def run_b200(args, world, rank, local):
             extras["other_algorithm"] = {"algorithm": ALGORITHM_NAMES[other],
                                          "value": batch * world / (msc / 1e3), "ms_per_step": msc}
             trc.destroy()
+        # Float32 pairwise products, Cl(6,0), batch 2^26: even-grade left operand
+        # (compact, 32 floats), dense right operand; HBM-bound sweep.
+        extras["pairwise_f32"] = pairwise_f32_leg(lib, args, world)
         # Same step on Cl(3,3) (the second signature of the headline config).
         X2, T2, w2 = X, T, w0
         tr33 = Trainer(lib, [1, 1, 1, -1, -1, -1], w2)
@@ -452,6 +497,8 @@ def run_b200(args, world, rank, local):
             line["e2e"] = extras["e2e"]
         if "cl33" in extras:
             line["cl33"] = extras["cl33"]
+        if "pairwise_f32" in extras:
+            line["pairwise_f32"] = extras["pairwise_f32"]
         if world == 1 and not args.no_extras:
             line["cpu_baseline"] = cpu_baseline_leg(q)
         print(json.dumps(line), flush=True)
@@ -471,6 +518,13 @@ def main():
         return
     world, rank, local = dist_setup(args.gpus)
     try:
+        if args.leg == "pairwise-f32":
+            from geometricelementaryoperators_b200 import abi
+
+            res = pairwise_f32_leg(abi.lib(), args, world)
+            if rank == 0:
+                print(json.dumps(res), flush=True)
+            return
         run_b200(args, world, rank, local)
     finally:
         if world > 1:

@@ -141,7 +141,7 @@ struct RepDevice {
     uint8_t grp_col[16][8];
     uint64_t grp_neg[16];
     int32_t blades, D, S, side;
-    int32_t raw_stride;  // padded row stride (doubles) of the staged raw tiles
+    int32_t raw_stride;  // row stride (doubles) of the staged raw tiles (= blades, unpadded)
     int32_t reserved;
 };
 bool make_rep_device(RepDevice *out, const RepPlan &plan);

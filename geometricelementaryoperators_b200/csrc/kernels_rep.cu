@@ -12,15 +12,19 @@
 // S*D*D GEMM: Cl(6,0)-type algebras use D = 16, S = 4 (1024 multiply-adds per
 // GEMM per sample instead of 4096), Cl(3,3)-type D = 8, S = 8 (512).
 //
-// Both GEMMs run on FP64 tensor cores with mma.sync.aligned.m16n8k4 (16-row
-// blocks of X' = 16/S samples per warp step; W' fragments stay in registers for
-// the whole kernel). GEMM 2 reads X'^T directly from shared memory as the A
-// operand, so no transpose is materialised. The signed gathers run on the FP64
-// pipe while other warps issue tensor-core work.
-//
-// HBM traffic per step = 2 x 8 x 2^n bytes per sample (x and t read once);
-// the padded shared-memory rows (D + 4 doubles) keep every fragment load at
-// two wavefronts.
+// Data movement per tile of TS samples (HBM traffic = x and t read once):
+//   * cp.async copies of the raw x and t rows into one of kStages shared-memory
+//     stages, issued kStages-1 tiles ahead (two CTAs per SM keep ~128 KB of
+//     loads in flight per SM);
+//   * gather in place: each thread loads the S blades of its blade group for
+//     its samples into registers, the CTA synchronises, then the S kept
+//     entries are written over the raw rows (a transformed sample is again
+//     2^n doubles), in an XOR-swizzled layout;
+//   * per 16-row block, a warp runs GEMM 1 with mma.sync.m16n8k4.f64 (W'
+//     fragments resident in registers), forms R' = Y' - T' in place, and GEMM 2
+//     reading X'^T straight from shared memory as the A operand.
+// The swizzles make every fragment load, every gather load and the epilogue
+// accesses hit each shared-memory bank at most twice per warp instruction.
 #include <cuda_runtime.h>
 #include <math.h>
 
@@ -28,11 +32,11 @@
 #include "representation.h"
 
 namespace geo {
-
 namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = 8;
+constexpr int kStages = 3;
 
 __device__ __forceinline__ void cp_async_16(void *smem, const void *gmem, int src_bytes) {
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -61,59 +65,53 @@ __device__ __forceinline__ void mma_16x8x4(double (&c)[4], double a0, double a1,
 
 template <int D, int S>
 struct RepGeo {
-    static constexpr int N = D * S;         // blades
-    static constexpr int LD = D + 4;        // padded row stride of X', T'/R' (doubles)
-    static constexpr int TS = (D == 8 && S == 8) ? 24 : 32;  // samples per tile (2 CTAs per SM fit)
+    static constexpr int N = D * S;         // blades (= doubles per sample, raw or transformed)
+    static constexpr int TS = 32;           // samples per tile
     static constexpr int ROWS = TS * S;     // X' rows per tile
     static constexpr int BLOCKS = ROWS / 16;
     static constexpr int NT = D / 8;        // 8-column tiles of the D outputs
     static constexpr int KT = D / 4;        // k-steps of GEMM 1
-    static constexpr int RAW = TS * (N + 8);  // doubles of one raw tile (padded rows)
+    static constexpr int TILE = TS * N;     // doubles of one raw tile (x or t)
+    static constexpr int STAGE = 2 * TILE;  // x tile + t tile
     static_assert(ROWS % 16 == 0 && D % 8 == 0, "tile shape");
 };
 
-template <int N, int TS, bool AL>
-__device__ __forceinline__ void stage_raw(double *dst, const double *__restrict__ src, size_t first, size_t batch,
-                                          int rs) {
+// Column swizzle of the transformed (X', T', R') rows, keyed by the row within
+// the tile: conflict-free GEMM-1 A loads (rows g, cols 4kt + t), GEMM-2 A/B
+// loads (rows 4kk + t, cols g) and 16-byte epilogue accesses.
+template <int D>
+__device__ __forceinline__ int xsw(int row) {
+    if (D == 16) return 4 * (2 * (row & 1) + ((row >> 2) & 1));
+    return 4 * ((row >> 1) & 1);
+}
+// Raw-row swizzle: for D = 8 (four samples per gather load) odd samples swap
+// their 64-byte halves so the four samples cover all 16 double-banks.
+template <int D>
+__device__ __forceinline__ int rsw(int sample) {
+    return D == 8 ? 8 * (sample & 1) : 0;
+}
+
+template <int D, int S, bool AL>
+__device__ __forceinline__ void stage_tile(double *dst, const double *__restrict__ src, size_t first, size_t batch) {
+    using G = RepGeo<D, S>;
+    constexpr int N = G::N;
     if (AL) {
-        for (int c = threadIdx.x; c < TS * (N / 2); c += kThreads) {
+        for (int c = threadIdx.x; c < G::TS * (N / 2); c += kThreads) {
             const int s = c / (N / 2);
-            const int k2 = c - s * (N / 2);
+            const int k = 2 * (c - s * (N / 2));
             const size_t sample = first + (size_t)s;
             const bool ok = sample < batch;
-            const double *g = ok ? src + sample * N + 2 * k2 : src;
-            cp_async_16(dst + s * rs + 2 * k2, g, ok ? 16 : 0);
+            const double *g = ok ? src + sample * N + k : src;
+            cp_async_16(dst + s * N + (k ^ rsw<D>(s)), g, ok ? 16 : 0);
         }
     } else {
-        for (int c = threadIdx.x; c < TS * N; c += kThreads) {
+        for (int c = threadIdx.x; c < G::TS * N; c += kThreads) {
             const int s = c / N;
             const int k = c - s * N;
             const size_t sample = first + (size_t)s;
             const bool ok = sample < batch;
             const double *g = ok ? src + sample * N + k : src;
-            cp_async_8(dst + s * rs + k, g, ok ? 8 : 0);
-        }
-    }
-}
-
-// Signed gather by blade group: the thread of group m loads each of its S
-// blades once and writes the S kept entries (s*S + r, grp_col[m][r]).
-template <int D, int S>
-__device__ __forceinline__ void gather(double *dst, const double *raw, int rs, int m, int slice,
-                                       const int (&blade)[S], const int (&col)[S], uint64_t neg) {
-    using G = RepGeo<D, S>;
-    constexpr int SLICES = kThreads / D;
-    for (int s = slice; s < G::TS; s += SLICES) {
-        const double *row = raw + s * rs;
-        double in[S];
-#pragma unroll
-        for (int t = 0; t < S; ++t) in[t] = row[blade[t]];
-#pragma unroll
-        for (int r = 0; r < S; ++r) {
-            double acc = 0.0;
-#pragma unroll
-            for (int t = 0; t < S; ++t) acc = ((neg >> (r * 8 + t)) & 1ull) ? acc - in[t] : acc + in[t];
-            dst[(s * S + r) * G::LD + col[r]] = acc;
+            cp_async_8(dst + s * N + (k ^ rsw<D>(s)), g, ok ? 8 : 0);
         }
     }
 }
@@ -123,19 +121,16 @@ __global__ void __launch_bounds__(kThreads, 2)
 rep_cycle_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ T,
                  const double *__restrict__ W, size_t batch, double *__restrict__ records) {
     using G = RepGeo<D, S>;
-    constexpr int N = G::N, LD = G::LD, TS = G::TS;
+    constexpr int N = G::N, TS = G::TS;
     extern __shared__ __align__(16) double smem[];
-    double *Wp = smem;                              // D*D
-    double *Xp = Wp + D * D;                        // ROWS*LD
-    double *Tp = Xp + G::ROWS * LD;                 // ROWS*LD (T', then R')
-    double *raw = Tp + G::ROWS * LD;                // 2 stages x (x tile, t tile), padded rows
-    const int rs = rep.raw_stride;
-    const int raw_tile = TS * rs;
+    double *Wp = smem;                     // D*D
+    double *stages = Wp + D * D;           // kStages x (x tile, t tile)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t4 = lane & 3;
 
     // This thread's blade group for the gathers, resident for the whole kernel.
+    constexpr int SLICES = kThreads / D;
     const int gm = threadIdx.x % D;
     const int gslice = threadIdx.x / D;
     int gblade[S], gcol[S];
@@ -145,6 +140,7 @@ rep_cycle_kernel(const RepDevice rep, const double *__restrict__ X, const double
         gcol[t] = rep.grp_col[gm][t];
     }
     const uint64_t gneg = rep.grp_neg[gm];
+
     // W' = rho(W) (right) or rho(W)^T (left): W'[k][j] = sum_{A: x_A = k^j} W_A sg_A (-1)^{z_A . col}
     for (int idx = threadIdx.x; idx < D * D; idx += kThreads) {
         const int k = idx / D, j = idx - k * D;
@@ -160,12 +156,17 @@ rep_cycle_kernel(const RepDevice rep, const double *__restrict__ X, const double
     }
 
     const size_t tiles = (batch + TS - 1) / TS;
-    size_t tile = blockIdx.x;
-    if (tile < tiles) {
-        stage_raw<N, TS, AL>(raw, X, tile * TS, batch, rs);
-        stage_raw<N, TS, AL>(raw + raw_tile, T, tile * TS, batch, rs);
+    // Prologue: issue the first kStages-1 tiles of this CTA.
+#pragma unroll
+    for (int st = 0; st < kStages - 1; ++st) {
+        const size_t tile = blockIdx.x + (size_t)st * gridDim.x;
+        if (tile < tiles) {
+            double *dst = stages + st * G::STAGE;
+            stage_tile<D, S, AL>(dst, X, tile * TS, batch);
+            stage_tile<D, S, AL>(dst + G::TILE, T, tile * TS, batch);
+        }
+        cp_async_commit();
     }
-    cp_async_commit();
     __syncthreads();
 
     // W' fragments for GEMM 1 (B operand, k-steps x n-tiles), resident all kernel.
@@ -175,42 +176,81 @@ rep_cycle_kernel(const RepDevice rep, const double *__restrict__ X, const double
 #pragma unroll
         for (int nt = 0; nt < G::NT; ++nt) bw[kt][nt] = Wp[(kt * 4 + t4) * D + nt * 8 + g];
 
-    // G' accumulators (this warp's partial): M = D rows in 16-row tiles, N = D cols in 8-col tiles.
-    constexpr int MT = (D + 15) / 16;  // 1 for D = 8 or 16 (D = 8 uses the top half only)
-    double gacc[MT][G::NT][4];
+    double gacc[G::NT][4];
 #pragma unroll
-    for (int m = 0; m < MT; ++m)
-#pragma unroll
-        for (int nt = 0; nt < G::NT; ++nt) gacc[m][nt][0] = gacc[m][nt][1] = gacc[m][nt][2] = gacc[m][nt][3] = 0.0;
+    for (int nt = 0; nt < G::NT; ++nt) gacc[nt][0] = gacc[nt][1] = gacc[nt][2] = gacc[nt][3] = 0.0;
     double sq = 0.0, check_y = 0.0, check_r = 0.0;
 
     int stage = 0;
-    for (; tile < tiles; tile += gridDim.x) {
-        const size_t next = tile + gridDim.x;
-        if (next < tiles) {
-            double *dst = raw + (stage ^ 1) * 2 * raw_tile;
-            stage_raw<N, TS, AL>(dst, X, next * TS, batch, rs);
-            stage_raw<N, TS, AL>(dst + raw_tile, T, next * TS, batch, rs);
+    for (size_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        // Issue the tile kStages-1 ahead into the stage freed at the end of the previous iteration.
+        {
+            const size_t ahead = tile + (size_t)(kStages - 1) * gridDim.x;
+            const int st = (stage + kStages - 1) % kStages;
+            if (ahead < tiles) {
+                double *dst = stages + st * G::STAGE;
+                stage_tile<D, S, AL>(dst, X, ahead * TS, batch);
+                stage_tile<D, S, AL>(dst + G::TILE, T, ahead * TS, batch);
+            }
+            cp_async_commit();
         }
-        cp_async_commit();
-        cp_async_wait<1>();
+        cp_async_wait<kStages - 1>();
         __syncthreads();
-        const double *rx = raw + stage * 2 * raw_tile;
-        gather<D, S>(Xp, rx, rs, gm, gslice, gblade, gcol, gneg);
-        gather<D, S>(Tp, rx + raw_tile, rs, gm, gslice, gblade, gcol, gneg);
+
+        double *xs = stages + stage * G::STAGE;
+        double *ts = xs + G::TILE;
+        // Gather in place: load this thread's blades of its samples, synchronise,
+        // write the kept entries over the same rows.
+        constexpr int PER = (TS + SLICES - 1) / SLICES;
+        double vx[PER][S], vt[PER][S];
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+            const int s = gslice + SLICES * i;
+            if (s < TS) {
+#pragma unroll
+                for (int t = 0; t < S; ++t) {
+                    const int col = gblade[t] ^ rsw<D>(s);
+                    vx[i][t] = xs[s * N + col];
+                    vt[i][t] = ts[s * N + col];
+                }
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+            const int s = gslice + SLICES * i;
+            if (s < TS) {
+#pragma unroll
+                for (int r = 0; r < S; ++r) {
+                    double ax = 0.0, at = 0.0;
+#pragma unroll
+                    for (int t = 0; t < S; ++t) {
+                        const bool neg = (gneg >> (r * 8 + t)) & 1ull;
+                        ax = neg ? ax - vx[i][t] : ax + vx[i][t];
+                        at = neg ? at - vt[i][t] : at + vt[i][t];
+                    }
+                    const int row = s * S + r;
+                    const int col = gcol[r] ^ xsw<D>(row);
+                    xs[row * D + col] = ax;
+                    ts[row * D + col] = at;
+                }
+            }
+        }
         __syncthreads();
 
         for (int blk = warp; blk < G::BLOCKS; blk += kWarps) {
-            const double *xb = Xp + blk * 16 * LD;
-            double *tb = Tp + blk * 16 * LD;
-            // GEMM 1: Y'(16 x D) = X'(16 x D) W'(D x D)
+            const double *xb = xs + blk * 16 * D;
+            double *tb = ts + blk * 16 * D;
+            // GEMM 1: Y'(16 x D) = X'(16 x D) W'(D x D). Block rows start at a multiple of 16,
+            // so the swizzle of local row r equals that of the tile row.
             double acc[G::NT][4];
 #pragma unroll
             for (int nt = 0; nt < G::NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0;
 #pragma unroll
             for (int kt = 0; kt < G::KT; ++kt) {
-                const double a0 = xb[g * LD + kt * 4 + t4];
-                const double a1 = xb[(g + 8) * LD + kt * 4 + t4];
+                const int c = kt * 4 + t4;
+                const double a0 = xb[g * D + (c ^ xsw<D>(g))];
+                const double a1 = xb[(g + 8) * D + (c ^ xsw<D>(g + 8))];
 #pragma unroll
                 for (int nt = 0; nt < G::NT; ++nt) mma_16x8x4(acc[nt], a0, a1, bw[kt][nt]);
             }
@@ -219,7 +259,8 @@ rep_cycle_kernel(const RepDevice rep, const double *__restrict__ X, const double
             for (int nt = 0; nt < G::NT; ++nt) {
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    double2 *p = reinterpret_cast<double2 *>(&tb[(g + 8 * h) * LD + nt * 8 + 2 * t4]);
+                    const int row = g + 8 * h;
+                    double2 *p = reinterpret_cast<double2 *>(&tb[row * D + ((nt * 8 + 2 * t4) ^ xsw<D>(row))]);
                     const double2 tv = *p;
                     double2 r;
                     r.x = acc[nt][2 * h] - tv.x;
@@ -235,51 +276,45 @@ rep_cycle_kernel(const RepDevice rep, const double *__restrict__ X, const double
             }
             __syncwarp();
             // GEMM 2: G'(D x D) += X'^T(D x 16) R'(16 x D); k runs over the 16 rows of the block.
+            // D = 8 uses the top half of the 16-row M tile (rows 8..15 of A are zero).
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
                 const int row = kk * 4 + t4;
+                const int sw = xsw<D>(row);
+                const double a0 = xb[row * D + (g ^ sw)];
+                const double a1 = (D >= 16) ? xb[row * D + ((g + 8) ^ sw)] : 0.0;
 #pragma unroll
-                for (int m = 0; m < MT; ++m) {
-                    const double a0 = xb[row * LD + m * 16 + g];
-                    const double a1 = (D >= 16) ? xb[row * LD + m * 16 + g + 8] : 0.0;
-#pragma unroll
-                    for (int nt = 0; nt < G::NT; ++nt) {
-                        const double b0 = tb[row * LD + nt * 8 + g];
-                        mma_16x8x4(gacc[m][nt], a0, a1, b0);
-                    }
+                for (int nt = 0; nt < G::NT; ++nt) {
+                    const double b0 = tb[row * D + ((nt * 8 + g) ^ sw)];
+                    mma_16x8x4(gacc[nt], a0, a1, b0);
                 }
             }
         }
-        __syncthreads();
-        stage ^= 1;
+        __syncthreads();  // the stage is reloaded by the next iteration's issue
+        stage = (stage + 1) % kStages;
     }
     cp_async_wait<0>();
     __syncthreads();
 
     // Reduce the warps' G' partials in warp order (deterministic) in shared memory.
-    // Buffers are free now: raw (>= 4*24*32 doubles) holds the kWarps x D x D
-    // partials, X' the summed D x D, T' the 3 x kThreads scalar partials.
-    static_assert(4 * G::TS * N >= kWarps * D * D && G::ROWS * LD >= D * D && G::ROWS * LD >= 3 * kThreads,
-                  "epilogue scratch fits");
-    double *Gs = raw;
+    double *Gs = stages;                            // kWarps * D * D
+    double *Gsum = Gs + kWarps * D * D;             // D * D
+    double *red = Gsum + D * D;                     // 3 * kThreads
+    static_assert(kWarps * D * D + D * D + 3 * kThreads <= kStages * G::STAGE, "epilogue scratch fits");
 #pragma unroll
-    for (int m = 0; m < MT; ++m)
+    for (int nt = 0; nt < G::NT; ++nt)
 #pragma unroll
-        for (int nt = 0; nt < G::NT; ++nt)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int row = m * 16 + g + 8 * h;
-                if (row < D) {
-                    Gs[(warp * D + row) * D + nt * 8 + 2 * t4] = gacc[m][nt][2 * h];
-                    Gs[(warp * D + row) * D + nt * 8 + 2 * t4 + 1] = gacc[m][nt][2 * h + 1];
-                }
+        for (int h = 0; h < 2; ++h) {
+            const int row = g + 8 * h;
+            if (row < D) {
+                Gs[(warp * D + row) * D + nt * 8 + 2 * t4] = gacc[nt][2 * h];
+                Gs[(warp * D + row) * D + nt * 8 + 2 * t4 + 1] = gacc[nt][2 * h + 1];
             }
-    double *red = Tp;  // 3 * kThreads doubles
+        }
     red[threadIdx.x] = sq;
     red[kThreads + threadIdx.x] = check_y;
     red[2 * kThreads + threadIdx.x] = check_r;
     __syncthreads();
-    double *Gsum = Xp;  // D * D
     for (int idx = threadIdx.x; idx < D * D; idx += kThreads) {
         double acc = 0.0;
         for (int w = 0; w < kWarps; ++w) acc += Gs[w * D * D + idx];
@@ -320,9 +355,9 @@ template <int D, int S, bool AL>
 cudaError_t launch_rep_impl(const RepDevice &rep, const double *X, const double *T, const double *W, size_t batch,
                             double *records, int *ctas_used, cudaStream_t stream) {
     using G = RepGeo<D, S>;
-    if (rep.raw_stride != G::N + 8 || rep.D != D || rep.S != S) return cudaErrorInvalidValue;
+    if (rep.raw_stride != G::N || rep.D != D || rep.S != S) return cudaErrorInvalidValue;
     auto kernel = rep_cycle_kernel<D, S, AL>;
-    const size_t smem = (size_t)(D * D + 2 * G::ROWS * G::LD + 4 * G::RAW) * sizeof(double);
+    const size_t smem = (size_t)(D * D + kStages * G::STAGE) * sizeof(double);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     int per_sm = 1;

@@ -19,6 +19,8 @@
 #include <math.h>
 #include <string.h>
 
+#include <utility>
+
 #include "geo/geo_b200.h"
 #include "geo_runtime.h"
 
@@ -127,6 +129,140 @@ pairwise_kernel(const geo::SignPlan plan, const T *__restrict__ left, int left_c
             out0[sample * N + b] = acc;
         }
     }
+}
+
+// ---- float32 n = 6 fast path ----------------------------------------------
+// One thread per element; the 64 output blades accumulate in registers and the
+// sign of every term is a compile-time constant of the canonical signature
+// Cl(6-Q, Q), so each term is one FFMA with a free operand negation. Tiles of
+// 64 elements are staged through padded shared memory with 16-byte copies
+// (coalesced in both directions); a compact even-grade left operand (32
+// floats per element) halves its read traffic.
+__host__ __device__ constexpr int popc_c(int v) { return v == 0 ? 0 : (v & 1) + popc_c(v >> 1); }
+
+// k-th even blade (increasing order) of a 6-dimensional algebra.
+__host__ __device__ constexpr int even_blade_c(int k) { return (k << 1) | (popc_c(k << 1) & 1); }
+
+__host__ __device__ constexpr int sign_c(int l, int r, int q) {
+    int s = 1;
+    for (int a = 0; a < 6; ++a) {
+        if ((l >> a) & 1) {
+            int lower = r & ((1 << a) - 1), c = 0;
+            for (; lower; lower &= lower - 1) ++c;
+            if (c & 1) s = -s;
+            if (((r >> a) & 1) && a >= 6 - q) s = -s;
+        }
+    }
+    return s;
+}
+
+// One term y[l^r] += +-a_l b_r with compile-time indices and sign; the whole
+// product is a fold over an index sequence so every array index is constant
+// (the operands stay in registers).
+template <int Q, bool COMPACT, int I, int LW>
+__device__ __forceinline__ void f32_term(const float (&a)[LW], const float (&b)[64], float (&y)[64]) {
+    constexpr int li = I / 64, r = I % 64;
+    constexpr int l = COMPACT ? even_blade_c(li) : li;
+    constexpr int sg = sign_c(l, r, Q);
+    y[l ^ r] = fmaf(sg > 0 ? a[li] : -a[li], b[r], y[l ^ r]);
+}
+
+template <int Q, bool COMPACT, int LW, int... I>
+__device__ __forceinline__ void f32_product(const float (&a)[LW], const float (&b)[64], float (&y)[64],
+                                            std::integer_sequence<int, I...>) {
+    (f32_term<Q, COMPACT, I, LW>(a, b, y), ...);
+}
+
+constexpr int kF32Threads = 64;
+constexpr int kF32LdR = 64 + 4;   // padded row stride (floats) of right / out tiles
+constexpr int kF32LdL = 64 + 4;   // left tile (dense or compact uses the first 32)
+
+template <int Q, bool COMPACT>
+__global__ void __launch_bounds__(kF32Threads)
+pairwise_f32_n6_kernel(const float *__restrict__ left, const float *__restrict__ right, float *__restrict__ out,
+                       size_t batch) {
+    constexpr int LW = COMPACT ? 32 : 64;
+    __shared__ __align__(16) float Ls[kF32Threads * kF32LdL];
+    __shared__ __align__(16) float Rs[kF32Threads * kF32LdR];
+    const int tid = threadIdx.x;
+    for (size_t first = (size_t)blockIdx.x * kF32Threads; first < batch; first += (size_t)gridDim.x * kF32Threads) {
+        const int rows = (int)min((size_t)kF32Threads, batch - first);
+        // stage: 16-byte chunks, consecutive threads take consecutive chunks
+        for (int c = tid; c < rows * (LW / 4); c += kF32Threads) {
+            const int s = c / (LW / 4), k = c - s * (LW / 4);
+            *reinterpret_cast<float4 *>(&Ls[s * kF32LdL + 4 * k]) =
+                *reinterpret_cast<const float4 *>(&left[(first + s) * LW + 4 * k]);
+        }
+        for (int c = tid; c < rows * 16; c += kF32Threads) {
+            const int s = c / 16, k = c - s * 16;
+            *reinterpret_cast<float4 *>(&Rs[s * kF32LdR + 4 * k]) =
+                *reinterpret_cast<const float4 *>(&right[(first + s) * 64 + 4 * k]);
+        }
+        __syncthreads();
+        float a[LW], b[64], y[64];
+        if (tid < rows) {
+#pragma unroll
+            for (int k = 0; k < LW / 4; ++k) {
+                const float4 v = *reinterpret_cast<const float4 *>(&Ls[tid * kF32LdL + 4 * k]);
+                a[4 * k] = v.x; a[4 * k + 1] = v.y; a[4 * k + 2] = v.z; a[4 * k + 3] = v.w;
+            }
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const float4 v = *reinterpret_cast<const float4 *>(&Rs[tid * kF32LdR + 4 * k]);
+                b[4 * k] = v.x; b[4 * k + 1] = v.y; b[4 * k + 2] = v.z; b[4 * k + 3] = v.w;
+            }
+#pragma unroll
+            for (int o = 0; o < 64; ++o) y[o] = 0.0f;
+            // y[l ^ r] += a_l b_r s(l, r); compact storage holds the even blades in increasing order
+            f32_product<Q, COMPACT, LW>(a, b, y, std::make_integer_sequence<int, LW * 64>{});
+        }
+        __syncthreads();
+        if (tid < rows) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+                *reinterpret_cast<float4 *>(&Rs[tid * kF32LdR + 4 * k]) =
+                    make_float4(y[4 * k], y[4 * k + 1], y[4 * k + 2], y[4 * k + 3]);
+        }
+        __syncthreads();
+        for (int c = tid; c < rows * 16; c += kF32Threads) {
+            const int s = c / 16, k = c - s * 16;
+            *reinterpret_cast<float4 *>(&out[(first + s) * 64 + 4 * k]) =
+                *reinterpret_cast<const float4 *>(&Rs[s * kF32LdR + 4 * k]);
+        }
+        __syncthreads();
+    }
+}
+
+// Canonical signature q of a length-6 signature (first 6-q entries +1, rest -1), or -1.
+int canonical_q6(const int8_t *sig) {
+    int q = 0;
+    while (q < 6 && sig[5 - q] == -1) ++q;
+    for (int a = 0; a < 6 - q; ++a)
+        if (sig[a] != 1) return -1;
+    return q;
+}
+
+bool launch_pairwise_f32_fast(const int8_t *signature, const float *left, int compact, const float *right, float *out,
+                              size_t batch, cudaStream_t stream, cudaError_t *err) {
+    const int q = canonical_q6(signature);
+    if (q < 0) return false;
+    const uintptr_t bits = (uintptr_t)left | (uintptr_t)right | (uintptr_t)out;
+    if (bits & 15u) return false;  // float4 paths need 16-byte alignment
+    size_t grid = (batch + kF32Threads - 1) / kF32Threads;
+    const size_t cap = (size_t)geo::device_sm_count() * 8;
+    if (grid > cap) grid = cap;
+#define GEO_F32_CASE(QQ)                                                                                       \
+    case QQ:                                                                                                   \
+        if (compact) pairwise_f32_n6_kernel<QQ, true><<<(unsigned)grid, kF32Threads, 0, stream>>>(left, right, out, batch); \
+        else pairwise_f32_n6_kernel<QQ, false><<<(unsigned)grid, kF32Threads, 0, stream>>>(left, right, out, batch); \
+        break;
+    switch (q) {
+        GEO_F32_CASE(0) GEO_F32_CASE(1) GEO_F32_CASE(2) GEO_F32_CASE(3) GEO_F32_CASE(4) GEO_F32_CASE(5) GEO_F32_CASE(6)
+        default: return false;
+    }
+#undef GEO_F32_CASE
+    *err = cudaGetLastError();
+    return true;
 }
 
 template <typename T, int MODE>
@@ -330,6 +466,13 @@ extern "C" geo_b200_status_t geo_b200_pairwise_gp_f32(uint8_t dimension, const i
                                                       const float *device_right, float *device_out, size_t batch,
                                                       cudaStream_t stream) {
     if (device_out == nullptr) return GEO_B200_INVALID_ARGUMENT;
+    if (dimension == 6 && signature != nullptr && device_left != nullptr && device_right != nullptr && batch > 0 &&
+        geo::signature_valid(signature, 6)) {
+        cudaError_t e = cudaSuccess;
+        if (launch_pairwise_f32_fast(signature, device_left, left_even_compact != 0, device_right, device_out, batch,
+                                     stream, &e))
+            return from_cuda(e);
+    }
     return launch_pairwise<float, kPairForward>(dimension, signature, device_left, left_even_compact != 0,
                                                 device_right, nullptr, nullptr, device_out, nullptr, batch, stream);
 }

@@ -218,11 +218,13 @@ bool make_rep_device(RepDevice *out, const RepPlan &p) {
     out->D = D;
     out->S = S;
     out->side = p.side;
-    // Bank classes: with 32 / D samples per warp instruction, rows padded so
-    // consecutive samples shift by 8 double-banks; a lane's load must then be
-    // distinct modulo `mod` among the D lanes of one sample.
+    // Bank classes: a warp's gather load covers 32 / D samples. Raw rows are
+    // unpadded; for D = 8 odd samples are stored with their 64-byte halves
+    // swapped (blade A at column A ^ 8), so four samples spread over all 16
+    // double-banks when the D lanes of one sample load blades distinct modulo 8.
+    // For D = 16 the 16 lanes of one sample need blades distinct modulo 16.
     const int mod = D >= 16 ? 16 : 8;
-    out->raw_stride = N + 8;
+    out->raw_stride = N;
     // Group members and their signs from the kept-entry gather table.
     std::vector<std::vector<int>> members(D);
     for (int A = 0; A < N; ++A) members[p.xm[A]].push_back(A);

@@ -262,8 +262,28 @@ def test_full_size_n6_properties(oracle, q):
         assert host(dloss)[0] == 0.0 and np.all(host(dgrad) == 0.0) and np.array_equal(host(dparam), w)
 
 
+def accurate_vjp(oracle, sig, x, cot, left: bool) -> np.ndarray:
+    """g_p = sum_i sigma(i,p) (X^T C)[i][i^p] with X^T C formed per 1024-sample chunk in
+    float64 and accumulated across chunks in extended precision (about 1e-15
+    relative to the result): a summation far more accurate than either the
+    reference's sequential sum or the GPU's tree."""
+    n = int(np.log2(x.shape[1]))
+    N = 1 << n
+    acc = np.zeros((N, N), dtype=np.longdouble)
+    for a in range(0, x.shape[0], 1024):
+        acc += (x[a:a + 1024].T @ cot[a:a + 1024]).astype(np.longdouble)
+    g = np.zeros(N, dtype=np.longdouble)
+    for p in range(N):
+        for i in range(N):
+            s = oracle.sign(p, i, sig) if left else oracle.sign(i, p, sig)
+            g[p] += s * acc[i, i ^ p]
+    return g.astype(np.float64)
+
+
 def test_n6_oracle_at_scale(oracle):
-    """2^16 samples of Cl(6,0) and Cl(3,3) against the full oracle (VJP sums 65536 terms)."""
+    """2^16 samples of Cl(6,0) and Cl(3,3): the VJP (65536-sample sums) is within
+    1e-12 of an accurate re-summation, at least as close as the reference's own
+    sequential sum (which loses ~1e-10 on cancelled components at this size)."""
     L = _lib()
     B = 1 << 16
     for q in (0, 3):
@@ -276,4 +296,8 @@ def test_n6_oracle_at_scale(oracle):
             assert L.geo_batch_gp_cuda_parameter_vjp_f64(ctypes.byref(plan.dev), ptr(dx), ptr(dt), B, left, ptr(g),
                                                          stream()) == 0
             sync()
-            assert tol_close(host(g), oracle.vjp(sig, x, t, bool(left))[1], TOL)
+            exact = accurate_vjp(oracle, sig, x, t, bool(left))
+            seq = oracle.vjp(sig, x, t, bool(left))[1]
+            assert tol_close(host(g), exact, TOL), max_violation(host(g), exact, TOL)
+            assert np.max(np.abs(host(g) - exact)) <= np.max(np.abs(seq - exact)) + 1e-12
+            assert tol_close(seq, exact, 1e-9)
