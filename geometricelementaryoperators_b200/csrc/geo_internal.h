@@ -118,6 +118,13 @@ cudaError_t launch_finalize(const double *records, int ctas, const OptimizerArgs
 cudaError_t launch_reduce_records(const double *records, int count, double *out, cudaStream_t stream,
                                   int accumulate = 0);
 
+// Parameter VJP with one CTA per tile of vjp_tile_samples(blades) samples, so
+// it needs exactly ceil(batch / tile) records; fails with cudaErrorInvalidValue
+// (launching nothing) when that exceeds max_records.
+size_t vjp_tile_samples(int blades);
+cudaError_t launch_vjp_per_tile(const SignPlan &plan, const double *inputs, const double *cotangents, size_t batch,
+                                double *records, int max_records, int *ctas_used, cudaStream_t stream);
+
 // Finite check of a device array; ORs `bit` into *status when a value is not finite.
 cudaError_t launch_check_finite(const double *values, size_t count, uint32_t bit,
                                 uint32_t *status, cudaStream_t stream);

@@ -601,7 +601,68 @@ cudaError_t dispatch(const SignPlan &plan, const double *in, const double *aux, 
     }
 }
 
+// One CTA per tile (no persistent loop), so the record count is known from the
+// batch alone; used when the caller supplies a fixed-size record buffer.
+template <int N, bool AL>
+cudaError_t launch_tiled_vjp_per_tile(const SignPlan &plan, const double *in, const double *aux, size_t batch,
+                                      double *records, int max_records, int *ctas_used, cudaStream_t stream) {
+    using G = Tiled<N>;
+    auto kernel = tiled_kernel<N, kModeVjp, AL>;
+    const size_t tiles = (batch + G::TS - 1) / G::TS;
+    if (tiles < 1 || tiles > (size_t)max_records) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)(N * N + 4 * G::TILE_DOUBLES) * sizeof(double);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    kernel<<<(unsigned)tiles, kThreads, smem, stream>>>(plan, in, aux, nullptr, nullptr, batch, records);
+    if (ctas_used) *ctas_used = (int)tiles;
+    return cudaGetLastError();
+}
+
+template <int N>
+cudaError_t launch_small_vjp_per_tile(const SignPlan &plan, const double *in, const double *aux, size_t batch,
+                                      double *records, int max_records, int *ctas_used, cudaStream_t stream) {
+    const size_t blocks = (batch + kThreads - 1) / kThreads;
+    if (blocks < 1 || blocks > (size_t)max_records) return cudaErrorInvalidValue;
+    small_kernel<N, kModeVjp><<<(unsigned)blocks, kThreads, 0, stream>>>(plan, in, aux, nullptr, nullptr, batch,
+                                                                         records);
+    if (ctas_used) *ctas_used = (int)blocks;
+    return cudaGetLastError();
+}
+
 }  // namespace
+
+size_t vjp_tile_samples(int blades) {
+    switch (blades) {
+        case 2:
+        case 4: return kThreads;
+        case 8: return Tiled<8>::TS;
+        case 16: return Tiled<16>::TS;
+        case 32: return Tiled<32>::TS;
+        case 64: return Tiled<64>::TS;
+        default: return 0;
+    }
+}
+
+cudaError_t launch_vjp_per_tile(const SignPlan &plan, const double *inputs, const double *cotangents, size_t batch,
+                                double *records, int max_records, int *ctas_used, cudaStream_t stream) {
+    const bool al = (((uintptr_t)inputs | (uintptr_t)cotangents) & 15u) == 0u;
+    switch (plan.blades) {
+        case 2: return launch_small_vjp_per_tile<2>(plan, inputs, cotangents, batch, records, max_records, ctas_used, stream);
+        case 4: return launch_small_vjp_per_tile<4>(plan, inputs, cotangents, batch, records, max_records, ctas_used, stream);
+#define GEO_TILE_CASE(NB)                                                                                         \
+    case NB:                                                                                                      \
+        return al ? launch_tiled_vjp_per_tile<NB, true>(plan, inputs, cotangents, batch, records, max_records,   \
+                                                        ctas_used, stream)                                      \
+                  : launch_tiled_vjp_per_tile<NB, false>(plan, inputs, cotangents, batch, records, max_records,  \
+                                                         ctas_used, stream);
+        GEO_TILE_CASE(8)
+        GEO_TILE_CASE(16)
+        GEO_TILE_CASE(32)
+        GEO_TILE_CASE(64)
+#undef GEO_TILE_CASE
+        default: return cudaErrorInvalidValue;
+    }
+}
 
 int device_sm_count() {
     int dev = 0, count = 0;

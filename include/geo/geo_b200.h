@@ -181,6 +181,38 @@ int geo_b200_v8_batch_train_step(void *program, uint32_t input_node, uint32_t ta
                                  int optimizer, double learning_rate, double beta1, double beta2, double epsilon,
                                  double gradient_scale, double *loss_sum);
 
+/* ---- 2c. parameter VJP that allocates nothing -------------------------- */
+
+/* This entry point has no counterpart in the reference.
+ *
+ * Same result as geo_batch_gp_cuda_parameter_vjp_f64 (the summed parameter
+ * cotangent of the batched geometric product), for callers that cannot call
+ * cudaMalloc: hosts whose own allocator has reserved the device memory up
+ * front (so a further cudaMalloc fails), latency-critical loops that must not
+ * take the implicit device synchronisation of cudaMalloc/cudaFree, and plugin
+ * hosts that forbid device allocation after start-up. It takes no plan (a plan
+ * upload allocates); dimension and signature are given directly, all arrays
+ * are device memory supplied by the caller, and the call is asynchronous on
+ * `stream`.
+ *
+ * Its reduction scratch is one fixed array compiled into the library
+ * (GEO_B200_NOALLOC_RECORDS records of 576 bytes, about 1.2 MB), which every
+ * GPU that loads the library holds until the process exits. That bounds the
+ * batch: batch_size must not exceed GEO_B200_NOALLOC_MAX_BATCH (131072
+ * samples, any dimension); larger batches are rejected with
+ * GEO_B200_INVALID_ARGUMENT before anything is launched. The first call on each
+ * device looks up the array's device address (a one-time set-up per device);
+ * make that first call before any stream capture. All calls share the one
+ * array and every call overwrites the part it uses, so calls whose kernels
+ * overlap on the GPU (different streams without ordering) race; order them on
+ * one stream. */
+#define GEO_B200_NOALLOC_RECORDS 2048u
+#define GEO_B200_NOALLOC_MAX_BATCH 131072u
+geo_b200_status_t geo_b200_parameter_vjp_noalloc_f64(uint8_t dimension, const int8_t *signature,
+                                                     int parameter_on_left, const double *device_inputs,
+                                                     const double *device_output_cotangents, size_t batch_size,
+                                                     double *device_parameter_cotangent, cudaStream_t stream);
+
 /* ---- 3. pairwise products (both operands vary per element) ------------ */
 
 /* out[s] = left[s] * right[s]. */
