@@ -147,9 +147,23 @@ struct RepDevice {
     uint8_t grp_blade[16][8];
     uint8_t grp_col[16][8];
     uint64_t grp_neg[16];
+    // Butterfly gather of the warp-specialised kernel. A group's S x S sign
+    // block is a signed Walsh-Hadamard matrix: kept entry r of group m is
+    //   alpha(r) * sum_c beta(c) (-1)^{c . phi(r)} x[A(m, c)]
+    // over the coordinates c of the group's blades. Lane L (L = m for D = 16;
+    // L = 8 * parity + m for D = 8, parity = sample & 1) loads blade
+    // ws_blade[L][t] = A(m, t ^ delta_L) at step t, negates it when bit t of
+    // ws_in_neg[L] is set, runs the in-register Walsh transform, and writes
+    // transform output f to kept row ws_out_row[L][f], negated when bit f of
+    // ws_out_neg[L] is set. delta_L is chosen so that every load step of a
+    // half-warp covers 16 distinct double-banks of the unswizzled raw rows.
+    uint8_t ws_blade[16][8];
+    uint8_t ws_out_row[16][8];
+    uint8_t ws_in_neg[16];
+    uint8_t ws_out_neg[16];
     int32_t blades, D, S, side;
     int32_t raw_stride;  // row stride (doubles) of the staged raw tiles (= blades, unpadded)
-    int32_t reserved;
+    int32_t ws_ready;    // butterfly tables present (warp-specialised kernel usable)
 };
 bool make_rep_device(RepDevice *out, const RepPlan &plan);
 // True when a tensor-core kernel exists for the plan's (D, S).

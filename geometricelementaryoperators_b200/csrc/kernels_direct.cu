@@ -429,8 +429,18 @@ __device__ __forceinline__ void ordered_record_sum(const double *__restrict__ re
         const int chunk = (count + kRecParts - 1) / kRecParts;
         const int lo = part * chunk;
         const int hi = min(count, lo + chunk);
+        // Loads in batches of 8 (independent, in flight together); the sum
+        // itself stays sequential in record order.
         double acc = 0.0;
-        for (int c = lo; c < hi; ++c) acc += records[(size_t)c * kRecStride + slot];
+        int c = lo;
+        for (; c + 8 <= hi; c += 8) {
+            double v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = records[(size_t)(c + u) * kRecStride + slot];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc += v[u];
+        }
+        for (; c < hi; ++c) acc += records[(size_t)c * kRecStride + slot];
         parts[part * kRecStride + slot] = acc;
     }
     __syncthreads();

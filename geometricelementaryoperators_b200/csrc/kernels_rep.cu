@@ -29,6 +29,7 @@
 #include <math.h>
 
 #include "geo_internal.h"
+#include "rep_layout.h"
 #include "representation.h"
 
 namespace geo {
@@ -374,6 +375,355 @@ cudaError_t launch_rep_impl(const RepDevice &rep, const double *X, const double 
     return cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------------------
+// Warp-specialised kernel (16-byte aligned x and t).
+//
+// Warps 0-3 (producers) move data: one thread issues bulk copies
+// (cp.async.bulk, completion on an mbarrier per stage) of the raw x and t rows
+// of a tile, kWsStages - 2 tiles ahead; all producers then gather the tile in
+// place into X' and T' (ws_index layout). Warps 4-7 (consumers) run the math
+// on the previous tile meanwhile:
+//   GEMM 1 transposed, Y'^T = W'^T X'^T (W'^T fragments resident as the A
+//     operand), so each lane's accumulators hold Y'[n0 + 2t + h][g (+8)];
+//   R' = Y' - T' in registers: exactly the B fragment of GEMM 2 when the four
+//     k slots of an mma are the rows n0 + 2t + h (h = 0, 1);
+//   GEMM 2, G' += X'^T R', with X'^T loaded as the A operand.
+// Named barriers hand stages over (FULL: gathered, EMPTY: consumed); every
+// wait on an mbarrier is bounded and a wait that gives up marks the record as
+// failed (non-finite check value) while the barrier protocol carries on.
+constexpr int kWsAhead = kWsStages - 2;
+constexpr int kBarFull = 1;                          // + stage
+constexpr int kBarEmpty = kBarFull + kWsStages;      // + stage
+constexpr int kBarProducers = kBarEmpty + kWsStages;  // producers only
+static_assert(kBarProducers < 16, "named barrier ids");
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+__device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int count) {
+    asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// Bounded wait for the completion of phase `parity`; false when it gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
+    const unsigned a = smem_u32(bar);
+    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+        unsigned done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// D(8x8) += A(8x4) * B(4x8): a0 = A[g][t], b0 = B[t][g], c0,c1 = C[g][2t, 2t+1].
+__device__ __forceinline__ void mma_8x8x4(double (&c)[2], double a0, double b0) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};\n"
+                 : "+d"(c[0]), "+d"(c[1])
+                 : "d"(a0), "d"(b0));
+}
+
+// Exponent field of v (0x7ff00000 exactly when v is not finite).
+__device__ __forceinline__ unsigned exponent_bits(double v) { return (unsigned)__double2hiint(v) & 0x7ff00000u; }
+
+// v with its sign bit XORed by `mask` (0 or 0x80000000): an integer operation.
+__device__ __forceinline__ double flip_sign(double v, unsigned mask) {
+    return __hiloint2double(__double2hiint(v) ^ (int)mask, __double2loint(v));
+}
+
+// In-place Walsh-Hadamard transform: w[f] <- sum_t (-1)^{popc(t & f)} w[t].
+template <int S>
+__device__ __forceinline__ void walsh(double (&w)[S]) {
+#pragma unroll
+    for (int h = 1; h < S; h <<= 1)
+#pragma unroll
+        for (int a = 0; a < S; ++a)
+            if (!(a & h)) {
+                const double u = w[a], v = w[a | h];
+                w[a] = u + v;
+                w[a | h] = u - v;
+            }
+}
+
+template <int D, int S>
+__global__ void __launch_bounds__(kWsThreads, 2)
+rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ T,
+              const double *__restrict__ W, size_t batch, double *__restrict__ records) {
+    using G = WsGeo<D, S>;
+    constexpr int N = G::N, TS = G::TS;
+    extern __shared__ __align__(16) double smem[];
+    double *Wp = smem;                    // D * D
+    double *stages = Wp + D * D;          // kWsStages x (x tile, t tile)
+    uint64_t *bars = reinterpret_cast<uint64_t *>(stages + kWsStages * G::STAGE);
+    __shared__ unsigned s_gave_up;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t tiles = (batch + TS - 1) / TS;
+    const int K = (size_t)blockIdx.x < tiles ? (int)((tiles - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+
+    if (tid == 0) {
+        for (int s = 0; s < kWsStages; ++s) mbar_init(&bars[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        s_gave_up = 0u;
+    }
+    // W' = rho(W) (right) or rho(W)^T (left), as in rep_cycle_kernel.
+    for (int idx = tid; idx < D * D; idx += kWsThreads) {
+        const int k = idx / D, j = idx - k * D;
+        const int col = rep.side ? k : j;
+        double acc = 0.0;
+        for (int A = 0; A < N; ++A) {
+            if (rep.xm[A] != (k ^ j)) continue;
+            const double w = W[A];
+            const bool neg = (rep.sg[A] < 0) != ((__popc(rep.zm[A] & col) & 1) != 0);
+            acc += neg ? -w : w;
+        }
+        Wp[idx] = acc;
+    }
+    __syncthreads();
+
+    // Consumer state (also declared, unused, in the producer warps).
+    constexpr int PT = D / 8;  // 8-column tiles of G'
+    double gacc[PT][2][D == 16 ? 4 : 2];
+#pragma unroll
+    for (int p = 0; p < PT; ++p)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int i = 0; i < (D == 16 ? 4 : 2); ++i) gacc[p][h][i] = 0.0;
+    double sq = 0.0;
+    unsigned worst_exp = 0u;
+
+    if (warp < kWsProducers / 32) {
+        // ------------------------------------------------------------ producers
+        const int m = tid % D, slot = tid / D;
+        const int L = D == 8 ? (slot & 1) * 8 + m : m;
+        // Offsets within a stage for this thread's first sample (slot); sample
+        // slot + SLOTS * i adds SLOTS * i * N to both.
+        int roff[S], woff[S];
+        unsigned in_sign[S], out_sign[S];
+#pragma unroll
+        for (int t = 0; t < S; ++t) {
+            roff[t] = slot * N + rep.ws_blade[L][t];
+            in_sign[t] = ((rep.ws_in_neg[L] >> t) & 1u) << 31;
+            const int r = rep.ws_out_row[L][t];
+            woff[t] = ws_index<D>(slot * S + r, rep.grp_col[m][r]);
+            out_sign[t] = ((rep.ws_out_neg[L] >> t) & 1u) << 31;
+        }
+        auto issue = [&](int k) {
+            const size_t first = (blockIdx.x + (size_t)k * gridDim.x) * TS;
+            const size_t count = batch - first < (size_t)TS ? batch - first : (size_t)TS;
+            const unsigned bytes = (unsigned)(count * N * sizeof(double));
+            double *dst = stages + (k % kWsStages) * G::STAGE;
+            uint64_t *bar = &bars[k % kWsStages];
+            mbar_expect_tx(bar, 2u * bytes);
+            bulk_load(dst, X + first * N, bytes, bar);
+            bulk_load(dst + G::TILE, T + first * N, bytes, bar);
+        };
+        if (tid == 0)
+            for (int k = 0; k < K && k < kWsAhead; ++k) issue(k);
+        for (int k = 0; k < K; ++k) {
+            const int st = k % kWsStages;
+            const int ahead = k + kWsAhead;
+            if (ahead < K) {
+                // The stage of `ahead` last held tile ahead - kWsStages: wait until it is consumed.
+                if (ahead >= kWsStages) named_sync(kBarEmpty + ahead % kWsStages, kWsThreads);
+                if (tid == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                    issue(ahead);
+                }
+            }
+            if (!mbar_wait(&bars[st], (unsigned)((k / kWsStages) & 1))) atomicOr(&s_gave_up, 1u);
+            const size_t first = (blockIdx.x + (size_t)k * gridDim.x) * TS;
+            const int valid = batch - first < (size_t)TS ? (int)(batch - first) : TS;
+            double *xs = stages + st * G::STAGE;
+            double *ts = xs + G::TILE;
+            double vx[G::PER][S], vt[G::PER][S];
+#pragma unroll
+            for (int i = 0; i < G::PER; ++i) {
+                const bool ok = slot + G::SLOTS * i < valid;
+#pragma unroll
+                for (int t = 0; t < S; ++t) {
+                    vx[i][t] = ok ? xs[G::SLOTS * i * N + roff[t]] : 0.0;
+                    vt[i][t] = ok ? ts[G::SLOTS * i * N + roff[t]] : 0.0;
+                }
+            }
+            named_sync(kBarProducers, kWsProducers);  // every raw read is done before the in-place writes
+#pragma unroll
+            for (int i = 0; i < G::PER; ++i) {
+#pragma unroll
+                for (int t = 0; t < S; ++t) {
+                    vx[i][t] = flip_sign(vx[i][t], in_sign[t]);
+                    vt[i][t] = flip_sign(vt[i][t], in_sign[t]);
+                }
+                walsh<S>(vx[i]);
+                walsh<S>(vt[i]);
+#pragma unroll
+                for (int f = 0; f < S; ++f) {
+                    xs[G::SLOTS * i * N + woff[f]] = flip_sign(vx[i][f], out_sign[f]);
+                    ts[G::SLOTS * i * N + woff[f]] = flip_sign(vt[i][f], out_sign[f]);
+                }
+            }
+            named_arrive(kBarFull + st, kWsThreads);
+        }
+    } else {
+        // ------------------------------------------------------------ consumers
+        const int cw = warp - kWsProducers / 32;
+        const int g = lane >> 2, t4 = lane & 3;
+        constexpr int KT = D / 4;
+        double wa0[KT], wa1[KT];
+#pragma unroll
+        for (int kk = 0; kk < KT; ++kk) {
+            wa0[kk] = Wp[(4 * kk + t4) * D + g];
+            wa1[kk] = D == 16 ? Wp[(4 * kk + t4) * D + g + 8] : 0.0;
+        }
+        for (int k = 0; k < K; ++k) {
+            const int st = k % kWsStages;
+            named_sync(kBarFull + st, kWsThreads);
+            const double *xs = stages + st * G::STAGE;
+            const double *ts = xs + G::TILE;
+#pragma unroll
+            for (int j = 0; j < G::GPW; j += 2) {
+                int n0[2];
+                n0[0] = (cw * G::GPW + j) * 8;
+                n0[1] = n0[0] + 8;
+                if constexpr (D == 16) {
+                    double c[2][4];
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) c[q][0] = c[q][1] = c[q][2] = c[q][3] = 0.0;
+#pragma unroll
+                    for (int kk = 0; kk < KT; ++kk)
+#pragma unroll
+                        for (int q = 0; q < 2; ++q)
+                            mma_16x8x4(c[q], wa0[kk], wa1[kk], xs[ws_index<D>(n0[q] + g, 4 * kk + t4)]);
+#pragma unroll
+                    for (int q = 0; q < 2; ++q)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int row = n0[q] + 2 * t4 + h;
+                            const int plo = ws_index<D>(row, g), phi = ws_index<D>(row, g + 8);
+                            const double rlo = c[q][h] - ts[plo];
+                            const double rhi = c[q][2 + h] - ts[phi];
+                            sq = fma(rlo, rlo, sq);
+                            sq = fma(rhi, rhi, sq);
+                            worst_exp = max(worst_exp, max(exponent_bits(rlo), exponent_bits(rhi)));
+                            const double alo = xs[plo], ahi = xs[phi];
+                            mma_16x8x4(gacc[0][h], alo, ahi, rlo);
+                            mma_16x8x4(gacc[PT - 1][h], alo, ahi, rhi);
+                        }
+                } else {
+                    double c[2][2];
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) c[q][0] = c[q][1] = 0.0;
+#pragma unroll
+                    for (int kk = 0; kk < KT; ++kk)
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) mma_8x8x4(c[q], wa0[kk], xs[ws_index<D>(n0[q] + g, 4 * kk + t4)]);
+#pragma unroll
+                    for (int q = 0; q < 2; ++q)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int row = n0[q] + 2 * t4 + h;
+                            const int pos = ws_index<D>(row, g);
+                            const double r = c[q][h] - ts[pos];
+                            sq = fma(r, r, sq);
+                            worst_exp = max(worst_exp, exponent_bits(r));
+                            mma_8x8x4(gacc[0][h], xs[pos], r);
+                        }
+                }
+            }
+            if (k + kWsStages < K) named_arrive(kBarEmpty + st, kWsThreads);
+        }
+    }
+    __syncthreads();
+
+    // Reduce the consumer warps' G' partials in warp order (deterministic).
+    double *Gs = stages;                 // 4 * D * D
+    double *Gsum = Gs + 4 * D * D;       // D * D
+    double *red = Gsum + D * D;          // kWsThreads
+    static_assert(5 * D * D + kWsThreads <= kWsStages * G::STAGE, "epilogue scratch fits");
+    if (warp >= kWsProducers / 32) {
+        const int cw = warp - kWsProducers / 32;
+        const int g = lane >> 2, t4 = lane & 3;
+        double *gw = Gs + cw * D * D;
+#pragma unroll
+        for (int p = 0; p < PT; ++p)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                gw[g * D + p * 8 + 2 * t4 + i] = gacc[p][0][i] + gacc[p][1][i];
+                if constexpr (D == 16) gw[(g + 8) * D + p * 8 + 2 * t4 + i] = gacc[p][0][2 + i] + gacc[p][1][2 + i];
+            }
+    }
+    red[tid] = sq;
+    const int bad = __syncthreads_or(worst_exp == 0x7ff00000u);
+    for (int idx = tid; idx < D * D; idx += kWsThreads)
+        Gsum[idx] = ((Gs[idx] + Gs[D * D + idx]) + Gs[2 * D * D + idx]) + Gs[3 * D * D + idx];
+    for (int width = kWsThreads / 2; width > 0; width >>= 1) {
+        __syncthreads();
+        if (tid < width) red[tid] += red[tid + width];
+    }
+    __syncthreads();
+    double *rec = records + (size_t)blockIdx.x * kRecStride;
+    const double inv_s = 1.0 / (double)S;  // exact: S is a power of two
+    if (tid < N) {
+        const int A = tid;
+        const int xa = rep.xm[A], za = rep.zm[A];
+        double acc = 0.0;
+        for (int j = 0; j < D; ++j) {
+            const double v = rep.side ? Gsum[j * D + (j ^ xa)] : Gsum[(j ^ xa) * D + j];
+            acc += (__popc(za & j) & 1) ? -v : v;
+        }
+        rec[A] = (rep.sg[A] < 0 ? -acc : acc) * inv_s;
+    }
+    if (tid == 0) {
+        rec[kRecLoss] = 0.5 * red[0] * inv_s;
+        rec[kRecCheckY] = 0.0;
+        // Y' = R' + T' with T' finite, so a non-finite output shows in R'.
+        rec[kRecCheckR] = (bad || s_gave_up) ? __longlong_as_double(0x7ff8000000000000ll) : 0.0;
+        rec[kRecCheckIn] = 0.0;
+    }
+}
+
+template <int D, int S>
+cudaError_t launch_rep_ws(const RepDevice &rep, const double *X, const double *T, const double *W, size_t batch,
+                          double *records, int *ctas_used, cudaStream_t stream) {
+    using G = WsGeo<D, S>;
+    if (rep.raw_stride != G::N || rep.D != D || rep.S != S) return cudaErrorInvalidValue;
+    auto kernel = rep_ws_kernel<D, S>;
+    const size_t smem = (size_t)(D * D + kWsStages * G::STAGE) * sizeof(double) + kWsStages * sizeof(uint64_t);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kWsThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    const size_t tiles = (batch + G::TS - 1) / G::TS;
+    size_t grid = (size_t)device_sm_count() * (size_t)per_sm;
+    if (grid > (size_t)kMaxCtas) grid = kMaxCtas;
+    if (grid > tiles) grid = tiles;
+    if (grid < 1) grid = 1;
+    kernel<<<(unsigned)grid, kWsThreads, smem, stream>>>(rep, X, T, W, batch, records);
+    if (ctas_used) *ctas_used = (int)grid;
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 bool rep_supported(const RepDevice &rep) {
@@ -386,7 +736,7 @@ cudaError_t launch_rep_cycle(const RepDevice &rep, const double *X, const double
     const bool al = (((uintptr_t)X | (uintptr_t)T) & 15u) == 0u;
 #define GEO_REP_CASE(DD, SS)                                                                             \
     if (rep.D == DD && rep.S == SS)                                                                      \
-        return al ? launch_rep_impl<DD, SS, true>(rep, X, T, W, batch, records, ctas_used, stream)      \
+        return (al && rep.ws_ready) ? launch_rep_ws<DD, SS>(rep, X, T, W, batch, records, ctas_used, stream) \
                   : launch_rep_impl<DD, SS, false>(rep, X, T, W, batch, records, ctas_used, stream);
     GEO_REP_CASE(16, 4)
     GEO_REP_CASE(8, 8)

@@ -1,0 +1,47 @@
+// rep_layout.h -- tile geometry and shared-memory layout of the
+// warp-specialised representation kernel (kernels_rep.cu). Shared with the
+// host-side layout check (tests/c/rep_check.cpp), which replays every shared
+// memory access pattern of the kernel and requires 16 distinct double-banks
+// per half-warp (a warp's 8-byte access is served as two half-warps).
+#pragma once
+
+#if defined(__CUDACC__)
+#define GEO_LAYOUT_FN __host__ __device__ __forceinline__
+#else
+#define GEO_LAYOUT_FN inline
+#endif
+
+namespace geo {
+
+constexpr int kWsThreads = 256;    // 8 warps per CTA
+constexpr int kWsProducers = 128;  // warps 0-3: bulk loads and gathers
+constexpr int kWsStages = 6;       // shared-memory stages per CTA
+
+template <int D, int S>
+struct WsGeo {
+    static constexpr int N = D * S;                // blades = doubles per sample
+    static constexpr int ROWS = D == 16 ? 64 : 128;  // X' rows per tile
+    static constexpr int TS = ROWS / S;            // samples per tile
+    static constexpr int TILE = ROWS * D;          // doubles of one array (x or t) per stage
+    static constexpr int STAGE = 2 * TILE;         // x tile + t tile (16 KB)
+    static constexpr int GROUPS = ROWS / 8;        // 8-row groups of the GEMMs
+    static constexpr int GPW = GROUPS / 4;         // groups per consumer warp
+    static constexpr int SLOTS = kWsProducers / D; // sample slots of the producer threads
+    static constexpr int PER = TS / SLOTS;         // samples per producer thread per tile
+    static_assert(TILE == TS * N && PER * SLOTS == TS && GPW % 2 == 0, "tile shape");
+};
+
+// Position of entry (row, col) of a transformed tile (X' or T', D doubles per
+// row). D = 16: the 4-column blocks of a row are XOR-permuted by
+// f(row) = (row & 3) ^ ((row >> 2) & 1). D = 8: pairs of rows form 16-double
+// units whose entries are XOR-permuted by 4 * (unit & 3) ^ 8 * ((unit >> 2) & 1),
+// which may move an entry into the other row of its unit; the second term puts
+// consecutive samples of S = 8 rows (four units each) in opposite halves.
+template <int D>
+GEO_LAYOUT_FN int ws_index(int row, int col) {
+    if (D == 16) return row * 16 + (col ^ (4 * ((row & 3) ^ ((row >> 2) & 1))));
+    const int unit = row >> 1;
+    return 16 * unit + ((8 * (row & 1) + col) ^ (4 * (unit & 3)) ^ (8 * ((unit >> 2) & 1)));
+}
+
+}  // namespace geo

@@ -203,6 +203,154 @@ bool augment(int l, const std::vector<std::vector<std::pair<int, int>>> &adj, st
     return false;
 }
 
+// Edge-colours the bipartite multigraph (lane L) x (blade mod `mod`), where
+// lane L may load any blade of lanes[L], into `steps` perfect matchings:
+// matching t gives every lane its load at step t. The graph is regular, so a
+// perfect matching exists at every step (Koenig).
+bool colour_loads(const std::vector<std::vector<int>> &lanes, int mod, int steps, uint8_t (*order)[8]) {
+    std::vector<std::vector<int>> remaining = lanes;
+    const int L = (int)lanes.size();
+    for (int t = 0; t < steps; ++t) {
+        std::vector<std::vector<std::pair<int, int>>> adj(L);
+        for (int l = 0; l < L; ++l)
+            for (int i = 0; i < (int)remaining[l].size(); ++i) adj[l].push_back({remaining[l][i] % mod, i});
+        std::vector<int> match_r(mod, -1), edge_of_r(mod, -1);
+        for (int l = 0; l < L; ++l) {
+            std::vector<char> seen(mod, 0);
+            if (!augment(l, adj, match_r, edge_of_r, seen)) return false;
+        }
+        std::vector<int> take(L, -1);
+        for (int r = 0; r < mod; ++r)
+            if (match_r[r] >= 0) take[match_r[r]] = edge_of_r[r];
+        for (int l = 0; l < L; ++l) {
+            if (take[l] < 0) return false;
+            order[l][t] = (uint8_t)remaining[l][take[l]];
+            remaining[l].erase(remaining[l].begin() + take[l]);
+        }
+    }
+    return true;
+}
+
+// Sign bits of group m's gather for a load order: bit (r * 8 + t) set when
+// kept entry (r, rows[r] ^ m) takes blade order[t] with a minus sign.
+bool gather_signs(const RepPlan &p, int m, const uint8_t *order, uint64_t *neg_out) {
+    uint64_t neg = 0;
+    for (int r = 0; r < p.S; ++r) {
+        const int e = r * p.D + (p.rows[r] ^ m);
+        for (int t = 0; t < p.c; ++t) {
+            int sign = 0;
+            for (int u = 0; u < p.c; ++u)
+                if (p.gb[e][u] == order[t]) sign = p.gs[e][u];
+            if (sign == 0) return false;
+            if (sign < 0) neg |= (uint64_t)1 << (r * 8 + t);
+        }
+    }
+    *neg_out = neg;
+    return true;
+}
+
+// Coordinates of a group's blades: all groups share the subspace V of z-masks
+// of group 0 (the blades with x-mask 0), and group m's blades are
+// A(m, c) = A(m, 0) ^ sum_i c_i a_i with a_i the blade of group 0 whose z-mask
+// is the i-th basis vector of V.
+bool make_ws_tables(RepDevice *out, const RepPlan &p, const std::vector<std::vector<int>> &members) {
+    const int D = p.D, S = p.S;
+    int d = 0;
+    while ((1 << d) < S) ++d;
+    // Basis of V from group 0 (which contains the scalar blade, z = 0).
+    std::vector<int> basis_blade;
+    {
+        std::vector<unsigned> ech;
+        for (int A : members[0]) {
+            if (p.zm[A] == 0) continue;
+            std::vector<unsigned> e2 = ech;
+            if (independent(e2, p.zm[A])) {
+                ech = e2;
+                basis_blade.push_back(A);
+            }
+        }
+        if ((int)basis_blade.size() != d) return false;
+    }
+    auto blade_at = [&](int m, int c) {
+        int A = members[m][0];
+        for (int i = 0; i < d; ++i)
+            if ((c >> i) & 1) A ^= basis_blade[i];
+        return A;
+    };
+    auto sign_in_entry = [&](int r, int k, int A) {
+        const int e = r * D + k;
+        for (int u = 0; u < p.c; ++u)
+            if (p.gb[e][u] == A) return (int)p.gs[e][u];
+        return 0;
+    };
+    // Per group: alpha(r), beta(c), phi(r) with s(r, c) = alpha beta (-1)^{c . phi}.
+    std::vector<std::vector<int>> alpha(D, std::vector<int>(S)), beta(D, std::vector<int>(S)),
+        phi(D, std::vector<int>(S));
+    for (int m = 0; m < D; ++m) {
+        std::vector<std::vector<int>> s(S, std::vector<int>(S));
+        for (int c = 0; c < S; ++c) {
+            const int A = blade_at(m, c);
+            if (p.xm[A] != m) return false;
+            for (int r = 0; r < S; ++r) {
+                s[r][c] = sign_in_entry(r, p.rows[r] ^ m, A);
+                if (s[r][c] == 0) return false;
+            }
+        }
+        std::vector<char> seen(S, 0);
+        for (int r = 0; r < S; ++r) {
+            alpha[m][r] = s[r][0];
+            int f = 0;
+            for (int i = 0; i < d; ++i) {
+                const int chi = s[r][1 << i] * s[r][0] * s[0][1 << i] * s[0][0];
+                if (chi < 0) f |= 1 << i;
+            }
+            phi[m][r] = f;
+            if (seen[f]) return false;
+            seen[f] = 1;
+        }
+        for (int c = 0; c < S; ++c) beta[m][c] = s[0][c] * s[0][0];
+        for (int r = 0; r < S; ++r)
+            for (int c = 0; c < S; ++c) {
+                const int ch = (__builtin_popcount(c & phi[m][r]) & 1) ? -1 : 1;
+                if (alpha[m][r] * beta[m][c] * ch != s[r][c]) return false;
+            }
+    }
+    // delta per lane: 16 lanes of a half-warp need distinct banks (blade mod 16)
+    // at step 0; the loads of step t differ from step 0 by one common XOR, so
+    // every step is then conflict-free.
+    const int lanes = D == 8 ? 16 : D;
+    std::vector<std::vector<std::pair<int, int>>> adj(lanes);
+    for (int L = 0; L < lanes; ++L)
+        for (int delta = 0; delta < S; ++delta) adj[L].push_back({blade_at(L % D, delta) % 16, delta});
+    std::vector<int> match_r(16, -1), edge_of_r(16, -1);
+    for (int L = 0; L < lanes; ++L) {
+        std::vector<char> seen(16, 0);
+        if (!augment(L, adj, match_r, edge_of_r, seen)) return false;
+    }
+    std::vector<int> delta(lanes, -1);
+    for (int b = 0; b < 16; ++b)
+        if (match_r[b] >= 0) delta[match_r[b]] = edge_of_r[b];
+    for (int L = 0; L < lanes; ++L) {
+        if (delta[L] < 0) return false;
+        const int m = L % D;
+        uint8_t in_neg = 0, out_neg = 0;
+        for (int t = 0; t < S; ++t) {
+            const int c = t ^ delta[L];
+            out->ws_blade[L][t] = (uint8_t)blade_at(m, c);
+            if (beta[m][c] < 0) in_neg |= (uint8_t)(1u << t);
+        }
+        for (int r = 0; r < S; ++r) {
+            const int f = phi[m][r];
+            out->ws_out_row[L][f] = (uint8_t)r;
+            const int sg = alpha[m][r] * ((__builtin_popcount(delta[L] & f) & 1) ? -1 : 1);
+            if (sg < 0) out_neg |= (uint8_t)(1u << f);
+        }
+        out->ws_in_neg[L] = in_neg;
+        out->ws_out_neg[L] = out_neg;
+    }
+    return true;
+}
+
 }  // namespace
 
 bool make_rep_device(RepDevice *out, const RepPlan &p) {
@@ -218,56 +366,23 @@ bool make_rep_device(RepDevice *out, const RepPlan &p) {
     out->D = D;
     out->S = S;
     out->side = p.side;
-    // Bank classes: a warp's gather load covers 32 / D samples. Raw rows are
-    // unpadded; for D = 8 odd samples are stored with their 64-byte halves
-    // swapped (blade A at column A ^ 8), so four samples spread over all 16
-    // double-banks when the D lanes of one sample load blades distinct modulo 8.
-    // For D = 16 the 16 lanes of one sample need blades distinct modulo 16.
-    const int mod = D >= 16 ? 16 : 8;
     out->raw_stride = N;
-    // Group members and their signs from the kept-entry gather table.
     std::vector<std::vector<int>> members(D);
     for (int A = 0; A < N; ++A) members[p.xm[A]].push_back(A);
     for (int m = 0; m < D; ++m)
         if ((int)members[m].size() != c) return false;
-    // Edge-colour the c-regular bipartite multigraph (group m) x (blade mod `mod`)
-    // into c perfect matchings: matching t gives every group its load at step t.
-    std::vector<std::vector<int>> remaining = members;
-    for (int t = 0; t < c; ++t) {
-        std::vector<std::vector<std::pair<int, int>>> adj(D);
-        for (int m = 0; m < D; ++m)
-            for (int i = 0; i < (int)remaining[m].size(); ++i) adj[m].push_back({remaining[m][i] % mod, i});
-        std::vector<int> match_r(mod, -1), edge_of_r(mod, -1);
-        for (int m = 0; m < D; ++m) {
-            std::vector<char> seen(mod, 0);
-            if (!augment(m, adj, match_r, edge_of_r, seen)) return false;
-        }
-        std::vector<int> take(D, -1);
-        for (int r = 0; r < mod; ++r)
-            if (match_r[r] >= 0) take[match_r[r]] = edge_of_r[r];
-        for (int m = 0; m < D; ++m) {
-            if (take[m] < 0) return false;
-            out->grp_blade[m][t] = (uint8_t)remaining[m][take[m]];
-            remaining[m].erase(remaining[m].begin() + take[m]);
-        }
-    }
-    for (int m = 0; m < D; ++m) {
-        uint64_t neg = 0;
-        for (int r = 0; r < S; ++r) {
-            const int k = p.rows[r] ^ m;
-            out->grp_col[m][r] = (uint8_t)k;
-            const int e = r * D + k;
-            for (int t = 0; t < c; ++t) {
-                const int A = out->grp_blade[m][t];
-                int sign = 0;
-                for (int u = 0; u < c; ++u)
-                    if (p.gb[e][u] == A) sign = p.gs[e][u];
-                if (sign == 0) return false;
-                if (sign < 0) neg |= (uint64_t)1 << (r * 8 + t);
-            }
-        }
-        out->grp_neg[m] = neg;
-    }
+    for (int m = 0; m < D; ++m)
+        for (int r = 0; r < S; ++r) out->grp_col[m][r] = (uint8_t)(p.rows[r] ^ m);
+    // Synchronous kernel: a warp's gather load covers 32 / D samples. For D = 8
+    // odd samples are staged with their 64-byte halves swapped (blade A at
+    // column A ^ 8), so the D lanes of one sample need blades distinct modulo 8;
+    // for D = 16 the 16 lanes of one sample need blades distinct modulo 16.
+    if (!colour_loads(members, D >= 16 ? 16 : 8, c, out->grp_blade)) return false;
+    for (int m = 0; m < D; ++m)
+        if (!gather_signs(p, m, out->grp_blade[m], &out->grp_neg[m])) return false;
+    // Warp-specialised kernel: butterfly tables (the kernel exists for
+    // D = 16, S >= 2 and D = 8, S >= 4; without tables the synchronous kernel runs).
+    if ((D == 16 && S >= 2) || (D == 8 && S >= 4)) out->ws_ready = make_ws_tables(out, p, members) ? 1 : 0;
     return true;
 }
 

@@ -6,11 +6,89 @@
 #include <cstdio>
 #include <cstdlib>
 #include <random>
+#include <vector>
 
 #include "representation.h"
 #include "geo_internal.h"
+#include "rep_layout.h"
 
 using namespace geo;
+
+// 16 lanes of a half-warp hit 16 distinct double-banks (8-byte words mod 16).
+static bool distinct_banks(const int *addr) {
+    unsigned used = 0;
+    for (int l = 0; l < 16; ++l) used |= 1u << (addr[l] & 15);
+    return __builtin_popcount(used) == 16;
+}
+
+// Replays every shared-memory access of rep_ws_kernel<D, S> (producer raw
+// reads and in-place writes, consumer fragment loads) per half-warp, and checks
+// that the producers' writes cover each transformed entry exactly once.
+template <int D, int S>
+static const char *check_ws_layout(const RepDevice &dev) {
+    using G = WsGeo<D, S>;
+    constexpr int N = G::N;
+    std::vector<int> hits(G::TILE, 0);
+    for (int w = 0; w < kWsProducers / 32; ++w)
+        for (int i = 0; i < G::PER; ++i)
+            for (int h = 0; h < 2; ++h) {
+                for (int t = 0; t < S; ++t) {
+                    int rd[16], wr[16];
+                    for (int l = 0; l < 16; ++l) {
+                        const int tid = 32 * w + 16 * h + l;
+                        const int m = tid % D, slot = tid / D;
+                        const int L = D == 8 ? (slot & 1) * 8 + m : m;
+                        const int sm = slot + G::SLOTS * i;
+                        rd[l] = sm * N + dev.ws_blade[L][t];
+                        const int r = dev.ws_out_row[L][t];  // transform output t goes to kept row r
+                        wr[l] = ws_index<D>(sm * S + r, dev.grp_col[m][r]);
+                        if (wr[l] < 0 || wr[l] >= G::TILE) return "write outside the tile";
+                        hits[wr[l]] += 1;
+                        // The kernel writes at sm * N + (offset computed for i = 0).
+                        const int sm0 = slot;
+                        if (wr[l] - sm * N != ws_index<D>(sm0 * S + r, dev.grp_col[m][r]) - sm0 * N)
+                            return "write offset depends on the sample";
+                    }
+                    if (!distinct_banks(rd)) return "producer raw read conflicts";
+                    if (!distinct_banks(wr)) return "producer write conflicts";
+                }
+            }
+    for (int e = 0; e < G::TILE; ++e)
+        if (hits[e] != 1) return "producer writes do not cover the tile once";
+    for (int cw = 0; cw < 4; ++cw)
+        for (int j = 0; j < G::GPW; ++j) {
+            const int n0 = (cw * G::GPW + j) * 8;
+            for (int h = 0; h < 2; ++h) {
+                for (int kk = 0; kk < D / 4; ++kk) {
+                    int a[16];
+                    for (int l = 0; l < 16; ++l) {
+                        const int lane = 16 * h + l, g = lane >> 2, t = lane & 3;
+                        a[l] = ws_index<D>(n0 + g, 4 * kk + t);
+                    }
+                    if (!distinct_banks(a)) return "GEMM 1 operand conflicts";
+                }
+                for (int hh = 0; hh < 2; ++hh)
+                    for (int off = 0; off < D; off += 8) {
+                        int a[16];
+                        for (int l = 0; l < 16; ++l) {
+                            const int lane = 16 * h + l, g = lane >> 2, t = lane & 3;
+                            a[l] = ws_index<D>(n0 + 2 * t + hh, g + off);
+                        }
+                        if (!distinct_banks(a)) return "epilogue / GEMM 2 operand conflicts";
+                    }
+            }
+        }
+    return nullptr;
+}
+
+static const char *check_ws(const RepDevice &dev) {
+    if (!dev.ws_ready) return nullptr;
+    if (dev.D == 16 && dev.S == 4) return check_ws_layout<16, 4>(dev);
+    if (dev.D == 16 && dev.S == 2) return check_ws_layout<16, 2>(dev);
+    if (dev.D == 8 && dev.S == 8) return check_ws_layout<8, 8>(dev);
+    if (dev.D == 8 && dev.S == 4) return check_ws_layout<8, 4>(dev);
+    return nullptr;  // no warp-specialised kernel for this shape
+}
 
 int main() {
     std::mt19937_64 rng(5);
@@ -84,6 +162,38 @@ int main() {
                     unsigned used = 0;
                     for (int m = 0; m < D; ++m) used |= 1u << (dev.grp_blade[m][t] % mod);
                     if (__builtin_popcount(used) != D) { printf("FAIL bank classes n=%d q=%d\n", n, q); return 1; }
+                }
+                // The warp-specialised kernel's butterfly gather gives the same entries.
+                if (((D == 8 && S >= 4) || (D == 16 && S >= 2)) && !dev.ws_ready) {
+                    printf("FAIL no butterfly tables n=%d q=%d side=%d\n", n, q, side);
+                    return 1;
+                }
+                for (int L = 0; dev.ws_ready && L < (D == 8 ? 16 : D); ++L) {
+                    const int m = L % D;
+                    double w[8];
+                    for (int t = 0; t < S; ++t) {
+                        const double v = x[dev.ws_blade[L][t]];
+                        w[t] = ((dev.ws_in_neg[L] >> t) & 1) ? -v : v;
+                    }
+                    for (int hs = 1; hs < S; hs <<= 1)
+                        for (int a = 0; a < S; ++a)
+                            if (!(a & hs)) {
+                                const double u = w[a], v = w[a | hs];
+                                w[a] = u + v;
+                                w[a | hs] = u - v;
+                            }
+                    for (int f = 0; f < S; ++f) {
+                        const int r = dev.ws_out_row[L][f];
+                        const double got = ((dev.ws_out_neg[L] >> f) & 1) ? -w[f] : w[f];
+                        if (std::fabs(got - Xp[r * D + dev.grp_col[m][r]]) > 1e-12) {
+                            printf("FAIL ws butterfly n=%d q=%d side=%d\n", n, q, side);
+                            return 1;
+                        }
+                    }
+                }
+                if (const char *why = check_ws(dev)) {
+                    printf("FAIL ws layout n=%d q=%d side=%d: %s\n", n, q, side, why);
+                    return 1;
                 }
                 printf("n=%d q=%d side=%d D=%d S=%d err=%.1e\n", n, q, side, D, S, err);
                 ++cases;
