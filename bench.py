@@ -170,7 +170,11 @@ def make_data(lib, sig, batch, seed, left=0):
 
 ALGORITHM_NAMES = {1: "cayley", 2: "representation"}
 KERNEL_NAMES = {1: "tiled_kernel<64, cycle> (Cayley matrix, FP64 FMA)",
-                2: "rep_cycle_kernel (D x D representation, FP64 tensor cores)"}
+                2: "rep_ws_kernel<16, 4> (warp-specialised D x D representation, FP64 tensor cores)"}
+# DRAM bytes (read + write) per sample of each kernel family, from one ncu
+# capture of the same step on 2^20 samples (profiles/rep_ws_kernel_cl60_train_2p20.md,
+# profiles/tiled_kernel_n6_train_2p20.md); traffic grows with the samples processed.
+NCU_TRAFFIC_PER_SAMPLE = {1: (1.073777e9 + 6.1568e6) / 2**20, 2: (1.073927e9 + 4.560896e6) / 2**20}
 
 
 class Trainer:
@@ -470,7 +474,11 @@ def run_b200(args, world, rank, local):
     algo_bytes = batch * BYTES_PER_SAMPLE
     achieved = algo_bytes / (kernel_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                "frac": achieved / hbm_peak, "traffic": None, "peak_source": peak_src,
+                "frac": achieved / hbm_peak,
+                "traffic": NCU_TRAFFIC_PER_SAMPLE[tr.algorithm] * batch if args.negative == 0 else None,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum on 2^20 samples, "
+                                  "scaled to the launch's samples",
+                "peak_source": peak_src,
                 "kernel": KERNEL_NAMES[tr.algorithm] + " + record reduction, CUDA events on the launch stream",
                 "kernel_ms": kernel_ms,
                 "fp64_flops_achieved_tflops": batch * FLOPS_PER_SAMPLE / (kernel_ms / 1e3) / 1e12}

@@ -15,6 +15,8 @@
 // neg[l] set when e_l e_p = -e_(l^p)). Sparse plans bake, per term t, the
 // mask of sources whose sign is negative, so the inner loop is one bit test
 // and one FMA per term.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <string.h>
@@ -233,6 +235,183 @@ pairwise_f32_n6_kernel(const float *__restrict__ left, const float *__restrict__
     }
 }
 
+
+// ---- float32 n = 6, TMA-staged ---------------------------------------------
+// Same arithmetic as pairwise_f32_n6_kernel; the data moves by TMA. Each CTA
+// of 64 threads (one element each) runs a ring of kTmaStages stages: tensor
+// loads of 64-row boxes of the left (32 or 64 floats per row) and right
+// (64 floats) operands, 128-byte swizzled, kTmaAhead tiles ahead of the
+// compute; outputs are written back over the right operand's rows and leave
+// by tensor stores. Rows past the batch read as zeros and are not stored.
+constexpr int kTmaRows = 64;
+constexpr int kTmaStages = 4;
+constexpr int kTmaAhead = kTmaStages - 2;
+constexpr int kTmaSub = kTmaRows * 32;  // floats of one [64][32] box (8 KB)
+constexpr uint32_t kTmaWaitLimit = 1u << 22;
+
+__device__ unsigned g_pairwise_tma_wait_failures;
+
+template <bool COMPACT>
+struct TmaTile {
+    static constexpr int A_SUB = COMPACT ? 1 : 2;  // boxes of the left operand
+    static constexpr int STAGE = (A_SUB + 2) * kTmaSub;
+    static constexpr unsigned BYTES = STAGE * sizeof(float);
+    static constexpr size_t SMEM = (size_t)kTmaStages * BYTES + 1024;  // + alignment slack
+};
+
+// Float offset of (row, 4-float chunk j) in a [64][32] box stored with the
+// 128-byte swizzle: chunk j of row r sits at chunk j ^ (r & 7).
+__device__ __forceinline__ int sw128(int row, int chunk) { return row * 32 + ((chunk ^ (row & 7)) << 2); }
+
+__device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];\n" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int x, int y, const void *src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"(map),
+                 "r"(x), "r"(y), "r"(smem_u32(src))
+                 : "memory");
+}
+
+template <int Q, bool COMPACT>
+__global__ void __launch_bounds__(kTmaRows)
+pairwise_f32_n6_tma_kernel(const __grid_constant__ CUtensorMap map_left, const __grid_constant__ CUtensorMap map_right,
+                           const __grid_constant__ CUtensorMap map_out, size_t batch) {
+    using TT = TmaTile<COMPACT>;
+    constexpr int LW = COMPACT ? 32 : 64;
+    extern __shared__ unsigned char tma_raw[];
+    __shared__ __align__(8) uint64_t bars[kTmaStages];
+    float *base = reinterpret_cast<float *>(((uintptr_t)tma_raw + 1023) & ~(uintptr_t)1023);
+    const int tid = threadIdx.x;
+    const size_t tiles = (batch + kTmaRows - 1) / kTmaRows;
+    const int K = (size_t)blockIdx.x < tiles ? (int)((tiles - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+    if (tid == 0) {
+        for (int s = 0; s < kTmaStages; ++s)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_u32(&bars[s])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    __syncthreads();
+    auto issue = [&](int k) {
+        const int s = k % kTmaStages;
+        float *st = base + s * TT::STAGE;
+        const int y = (int)((blockIdx.x + (size_t)k * gridDim.x) * kTmaRows);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(&bars[s])),
+                     "r"(TT::BYTES)
+                     : "memory");
+        tma_load_2d(st, &map_left, 0, y, &bars[s]);
+        if (!COMPACT) tma_load_2d(st + kTmaSub, &map_left, 32, y, &bars[s]);
+        tma_load_2d(st + TT::A_SUB * kTmaSub, &map_right, 0, y, &bars[s]);
+        tma_load_2d(st + (TT::A_SUB + 1) * kTmaSub, &map_right, 32, y, &bars[s]);
+    };
+    if (tid == 0)
+        for (int k = 0; k < K && k < kTmaAhead; ++k) issue(k);
+    for (int k = 0; k < K; ++k) {
+        const int s = k % kTmaStages;
+        if (tid == 0 && k + kTmaAhead < K) {
+            // The stage of tile k + kTmaAhead last held tile k - 2, whose store
+            // must have finished reading it; the store of tile k - 1 may still run.
+            asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
+            issue(k + kTmaAhead);
+        }
+        {
+            const unsigned a = smem_u32(&bars[s]), parity = (unsigned)((k / kTmaStages) & 1);
+            bool ok = false;
+            for (uint32_t i = 0; i < kTmaWaitLimit && !ok; ++i) {
+                unsigned done;
+                asm volatile(
+                    "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, "
+                    "p;\n}\n"
+                    : "=r"(done)
+                    : "r"(a), "r"(parity)
+                    : "memory");
+                ok = done != 0;
+            }
+            if (!ok) atomicAdd(&g_pairwise_tma_wait_failures, 1u);
+        }
+        float *st = base + s * TT::STAGE;
+        float *rb = st + TT::A_SUB * kTmaSub;
+        float a[LW], b[64], y[64];
+#pragma unroll
+        for (int j = 0; j < LW / 4; ++j) {
+            const float4 v = *reinterpret_cast<const float4 *>(&st[(j >> 3) * kTmaSub + sw128(tid, j & 7)]);
+            a[4 * j] = v.x; a[4 * j + 1] = v.y; a[4 * j + 2] = v.z; a[4 * j + 3] = v.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const float4 v = *reinterpret_cast<const float4 *>(&rb[(j >> 3) * kTmaSub + sw128(tid, j & 7)]);
+            b[4 * j] = v.x; b[4 * j + 1] = v.y; b[4 * j + 2] = v.z; b[4 * j + 3] = v.w;
+        }
+#pragma unroll
+        for (int o = 0; o < 64; ++o) y[o] = 0.0f;
+        f32_product<Q, COMPACT, LW>(a, b, y, std::make_integer_sequence<int, LW * 64>{});
+        // Each thread overwrites only its own row, which only it has read.
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            *reinterpret_cast<float4 *>(&rb[(j >> 3) * kTmaSub + sw128(tid, j & 7)]) =
+                make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        __syncthreads();
+        if (tid == 0) {
+            const int row = (int)((blockIdx.x + (size_t)k * gridDim.x) * kTmaRows);
+            tma_store_2d(&map_out, 0, row, rb);
+            tma_store_2d(&map_out, 32, row, rb + kTmaSub);
+            asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+        }
+    }
+    if (tid == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+}
+
+// cuTensorMapEncodeTiled from the driver (resolved once; null when unavailable).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            (void)cudaGetLastError();
+            return nullptr;
+        }
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// [rows][cols] float32 tensor, 64 x 32 boxes, 128-byte swizzle, zero fill.
+bool encode_rows(CUtensorMap *map, const float *ptr, int cols, size_t rows) {
+    const auto encode = tensor_map_encoder();
+    if (encode == nullptr || rows == 0 || rows > 0xffffffffull) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * sizeof(float)};
+    const cuuint32_t box[2] = {32, (cuuint32_t)kTmaRows};
+    const cuuint32_t elem[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int Q, bool COMPACT>
+cudaError_t launch_f32_tma(const CUtensorMap &ml, const CUtensorMap &mr, const CUtensorMap &mo, size_t batch,
+                           cudaStream_t stream) {
+    auto kernel = pairwise_f32_n6_tma_kernel<Q, COMPACT>;
+    const size_t smem = TmaTile<COMPACT>::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kTmaRows, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    const size_t tiles = (batch + kTmaRows - 1) / kTmaRows;
+    size_t grid = (size_t)geo::device_sm_count() * (size_t)per_sm;
+    if (grid > tiles) grid = tiles;
+    kernel<<<(unsigned)grid, kTmaRows, smem, stream>>>(ml, mr, mo, batch);
+    return cudaGetLastError();
+}
+
 // Canonical signature q of a length-6 signature (first 6-q entries +1, rest -1), or -1.
 int canonical_q6(const int8_t *sig) {
     int q = 0;
@@ -248,6 +427,23 @@ bool launch_pairwise_f32_fast(const int8_t *signature, const float *left, int co
     if (q < 0) return false;
     const uintptr_t bits = (uintptr_t)left | (uintptr_t)right | (uintptr_t)out;
     if (bits & 15u) return false;  // float4 paths need 16-byte alignment
+    {
+        CUtensorMap ml, mr, mo;
+        if (encode_rows(&ml, left, compact ? 32 : 64, batch) && encode_rows(&mr, right, 64, batch) &&
+            encode_rows(&mo, out, 64, batch)) {
+#define GEO_F32_TMA_CASE(QQ)                                                                        \
+    case QQ:                                                                                        \
+        *err = compact ? launch_f32_tma<QQ, true>(ml, mr, mo, batch, stream)                       \
+                       : launch_f32_tma<QQ, false>(ml, mr, mo, batch, stream);                     \
+        return true;
+            switch (q) {
+                GEO_F32_TMA_CASE(0) GEO_F32_TMA_CASE(1) GEO_F32_TMA_CASE(2) GEO_F32_TMA_CASE(3) GEO_F32_TMA_CASE(4)
+                GEO_F32_TMA_CASE(5) GEO_F32_TMA_CASE(6)
+                default: break;
+            }
+#undef GEO_F32_TMA_CASE
+        }
+    }
     size_t grid = (batch + kF32Threads - 1) / kF32Threads;
     const size_t cap = (size_t)geo::device_sm_count() * 8;
     if (grid > cap) grid = cap;

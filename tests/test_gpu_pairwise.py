@@ -36,30 +36,59 @@ def test_pairwise_f64_all_signatures(oracle):
         assert tol_close(host(jt), jv, TOL)
 
 
+@pytest.mark.parametrize("q", [0, 3, 6])
 @pytest.mark.parametrize("compact", [0, 1])
-def test_pairwise_f32_even_operand(oracle, compact):
-    """Cl(6,0) float32 build: even-grade left operand (32 blades, N(0,1)), dense right U[-1,1];
-    float64 oracle at 1e-5."""
+def test_pairwise_f32_even_operand(oracle, compact, q):
+    """Cl(6-q,q) float32 build: even-grade left operand (32 blades, N(0,1)), dense right U[-1,1];
+    float64 oracle at 1e-5. The batch ends inside a 64-row tile; rows past it stay untouched."""
     import torch
 
     L = abi.lib()
-    sig = canonical_signature(6, 0)
+    sig = canonical_signature(6, q)
     B = 3001
     even = np.array([b for b in range(64) if bin(b).count("1") % 2 == 0])
     a = np.zeros((B, 64))
-    a[:, even] = normal(61, (B, 32))
-    b = splitmix_uniform(62, (B, 64))
+    a[:, even] = normal(61 + q, (B, 32))
+    b = splitmix_uniform(62 + q, (B, 64))
     a32 = a.astype(np.float32)
     b32 = b.astype(np.float32)
     left = a32[:, even] if compact else a32
     dl = torch.from_numpy(np.ascontiguousarray(left)).cuda()
     dr = torch.from_numpy(b32).cuda()
-    out = torch.zeros((B, 64), dtype=torch.float32, device="cuda")
+    out = torch.full((B + 64, 64), 7.0, dtype=torch.float32, device="cuda")
     assert L.geo_b200_pairwise_gp_f32(6, abi.sig_array(sig), ptr(dl), compact, ptr(dr), ptr(out), B, stream()) == 0
     sync()
     want = np.stack([oracle.gp(sig, a32[i].astype(np.float64), b32[i].astype(np.float64)) for i in range(B)])
     got = host(out).astype(np.float64)
-    assert tol_close(got, want, TOL_F32), max_violation(got, want, TOL_F32)
+    assert tol_close(got[:B], want, TOL_F32), max_violation(got[:B], want, TOL_F32)
+    assert np.all(got[B:] == 7.0)
+
+
+def test_pairwise_f32_full_size_spot_rows(oracle):
+    """Float32 sweep shape (compact even left, 2^22 + 5 pairs): spot rows, first and last tiles included."""
+    import torch
+
+    L = abi.lib()
+    sig = canonical_signature(6, 0)
+    B = (1 << 22) + 5
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    dl = torch.randn((B, 32), dtype=torch.float32, device="cuda", generator=gen)
+    dr = torch.rand((B, 64), dtype=torch.float32, device="cuda", generator=gen).mul_(2).sub_(1)
+    out = torch.full((B + 3, 64), 7.0, dtype=torch.float32, device="cuda")
+    assert L.geo_b200_pairwise_gp_f32(6, abi.sig_array(sig), ptr(dl), 1, ptr(dr), ptr(out), B, stream()) == 0
+    sync()
+    rows = np.unique(np.concatenate([np.arange(70), np.arange(B - 70, B),
+                                     np.random.default_rng(3).integers(0, B, 500)]))
+    even = np.array([b for b in range(64) if bin(b).count("1") % 2 == 0])
+    al = host(dl[rows]).astype(np.float64)
+    br = host(dr[rows]).astype(np.float64)
+    got = host(out[rows]).astype(np.float64)
+    for i in range(len(rows)):
+        a = np.zeros(64)
+        a[even] = al[i]
+        want = oracle.gp(sig, a, br[i])
+        assert tol_close(got[i], want, TOL_F32), (rows[i], max_violation(got[i], want, TOL_F32))
+    assert np.all(host(out[B:]) == 7.0)
 
 
 def test_sparse_plans(oracle):
