@@ -240,12 +240,14 @@ pairwise_f32_n6_kernel(const float *__restrict__ left, const float *__restrict__
 // Same arithmetic as pairwise_f32_n6_kernel; the data moves by TMA. Each CTA
 // of 64 threads (one element each) runs a ring of kTmaStages stages: tensor
 // loads of 64-row boxes of the left (32 or 64 floats per row) and right
-// (64 floats) operands, 128-byte swizzled, kTmaAhead tiles ahead of the
-// compute; outputs are written back over the right operand's rows and leave
-// by tensor stores. Rows past the batch read as zeros and are not stored.
+// (64 floats) operands, 128-byte swizzled; outputs are written back over the
+// right operand's rows and leave by tensor stores. At the top of iteration k
+// the stage of tile k - 1 is refilled with tile k + 2 once its store has
+// read it, so two tiles are in flight during each compute. Three stages keep
+// three CTAs (six warps) per SM for the compact left operand. Rows past the
+// batch read as zeros and are not stored.
 constexpr int kTmaRows = 64;
-constexpr int kTmaStages = 4;
-constexpr int kTmaAhead = kTmaStages - 2;
+constexpr int kTmaStages = 3;
 constexpr int kTmaSub = kTmaRows * 32;  // floats of one [64][32] box (8 KB)
 constexpr uint32_t kTmaWaitLimit = 1u << 22;
 
@@ -309,14 +311,14 @@ pairwise_f32_n6_tma_kernel(const __grid_constant__ CUtensorMap map_left, const _
         tma_load_2d(st + (TT::A_SUB + 1) * kTmaSub, &map_right, 32, y, &bars[s]);
     };
     if (tid == 0)
-        for (int k = 0; k < K && k < kTmaAhead; ++k) issue(k);
+        for (int k = 0; k < K && k < kTmaStages; ++k) issue(k);
     for (int k = 0; k < K; ++k) {
         const int s = k % kTmaStages;
-        if (tid == 0 && k + kTmaAhead < K) {
-            // The stage of tile k + kTmaAhead last held tile k - 2, whose store
-            // must have finished reading it; the store of tile k - 1 may still run.
-            asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
-            issue(k + kTmaAhead);
+        if (tid == 0 && k >= 1 && k + kTmaStages - 1 < K) {
+            // The stage of tile k + 2 last held tile k - 1, whose store (the
+            // latest one) must have finished reading it.
+            asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+            issue(k + kTmaStages - 1);
         }
         {
             const unsigned a = smem_u32(&bars[s]), parity = (unsigned)((k / kTmaStages) & 1);
