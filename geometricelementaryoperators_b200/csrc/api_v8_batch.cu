@@ -12,6 +12,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <vector>
 
 #include "geo/full_cycle_v8.h"
 #include "geo/geo_b200.h"
@@ -77,7 +78,45 @@ struct Workspace {
 };
 Workspace g_ws[64];
 
+// Any other graph: per-sample forward/backward on the GPU (v8_batch.cu), the
+// summed leaf gradients written into the program, then the program's own
+// optimizer step (constraints and transactionality included).
+int general_step(geo_v8_program_t *p, uint32_t input_node, uint32_t target_node, const double *device_inputs,
+                 const double *device_targets, size_t batch, int optimizer, double learning_rate, double beta1,
+                 double beta2, double epsilon, double gradient_scale, double *loss_sum) {
+    if (!is_kind(p, input_node, GEO_V8_NODE_INPUT)) return GEO_V8_BAD_PROGRAM;
+    if (target_node != GEO_V8_INVALID_NODE && !is_kind(p, target_node, GEO_V8_NODE_TARGET)) return GEO_V8_BAD_PROGRAM;
+    (void)geo_v8_zero_grad(p);
+    double loss = 0.0;
+    std::vector<double> grads;
+    const geo_v8_status_t st = geo::v8::run_batch(p, input_node, target_node, GEO_V8_INVALID_NODE, device_inputs,
+                                                  target_node != GEO_V8_INVALID_NODE ? device_targets : nullptr,
+                                                  nullptr, batch, 1, &loss, &grads);
+    if (st != GEO_V8_OK) return st;
+    const size_t blades = (size_t)1 << p->dimension;
+    for (geo_v8_node_id_t i = 0; i < p->node_count; ++i)
+        if (geo::v8::leaf_kind(p->nodes[i].kind) && p->nodes[i].requires_grad)
+            memcpy(p->nodes[i].gradient.coefficients, &grads[(size_t)i * 64], blades * sizeof(double));
+    p->gradient_samples = batch > 0xffffffffull ? 0xffffffffu : (uint32_t)batch;
+    p->forward_valid = 1u;
+    p->backward_valid = 1u;
+    if (loss_sum) *loss_sum = loss;
+    return geo_v8_optimizer_step(p, (geo_v8_optimizer_t)optimizer, learning_rate, beta1, beta2, epsilon,
+                                 gradient_scale);
+}
+
 }  // namespace
+
+extern "C" int geo_b200_v8_batch_forward(void *program_ptr, uint32_t input_node, const double *device_inputs,
+                                         size_t batch, uint32_t output_node, double *device_outputs) {
+    geo_v8_program_t *p = (geo_v8_program_t *)program_ptr;
+    if (!geo::v8::program_valid(p)) return GEO_V8_BAD_PROGRAM;
+    if (!p->compiled) return GEO_V8_NOT_COMPILED;
+    if (device_inputs == nullptr || device_outputs == nullptr || batch == 0) return GEO_V8_INVALID_ARGUMENT;
+    if (!is_kind(p, input_node, GEO_V8_NODE_INPUT) || output_node >= p->node_count) return GEO_V8_BAD_PROGRAM;
+    return geo::v8::run_batch(p, input_node, GEO_V8_INVALID_NODE, output_node, device_inputs, nullptr,
+                              device_outputs, batch, 0, nullptr, nullptr);
+}
 
 extern "C" int geo_b200_v8_batch_train_step(void *program_ptr, uint32_t input_node, uint32_t target_node,
                                             const double *device_inputs, const double *device_targets,
@@ -86,14 +125,17 @@ extern "C" int geo_b200_v8_batch_train_step(void *program_ptr, uint32_t input_no
     geo_v8_program_t *p = (geo_v8_program_t *)program_ptr;
     if (!geo::v8::program_valid(p)) return GEO_V8_BAD_PROGRAM;
     if (!p->compiled) return GEO_V8_NOT_COMPILED;
-    if (device_inputs == nullptr || device_targets == nullptr || batch == 0) return GEO_V8_INVALID_ARGUMENT;
+    if (device_inputs == nullptr || batch == 0 || (device_targets == nullptr && target_node != GEO_V8_INVALID_NODE))
+        return GEO_V8_INVALID_ARGUMENT;
     if ((optimizer != GEO_V8_OPTIMIZER_SGD && optimizer != GEO_V8_OPTIMIZER_ADAM) || !isfinite(learning_rate) ||
         learning_rate <= 0.0 || !isfinite(gradient_scale) || gradient_scale <= 0.0 || !isfinite(beta1) ||
         beta1 < 0.0 || beta1 >= 1.0 || !isfinite(beta2) || beta2 < 0.0 || beta2 >= 1.0 || !isfinite(epsilon) ||
         epsilon <= 0.0)
         return GEO_V8_INVALID_ARGUMENT;
     Match m;
-    if (!match(p, input_node, target_node, &m)) return GEO_V8_BAD_PROGRAM;
+    if (!match(p, input_node, target_node, &m))
+        return general_step(p, input_node, target_node, device_inputs, device_targets, batch, optimizer,
+                            learning_rate, beta1, beta2, epsilon, gradient_scale, loss_sum);
     geo_v8_node_t *param = &p->nodes[m.param];
     if (!geo::v8::mv_valid(&param->value, p->dimension, p->signature)) return GEO_V8_NUMERIC_FAILURE;
 

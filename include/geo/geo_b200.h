@@ -164,22 +164,35 @@ geo_b200_status_t geo_b200_trainer_attach_comm(geo_b200_trainer_t *trainer, geo_
 
 /* One optimizer step of a compiled V8 program over a device-resident
  * minibatch, equal to: geo_v8_zero_grad; for every sample s: set the INPUT
- * node to inputs[s] and the TARGET node to targets[s], geo_v8_forward,
- * geo_v8_backward(accumulate = s != 0); then geo_v8_optimizer_step(optimizer,
- * ..., gradient_scale). The program must be the graph
- *   gp = GEOMETRIC_PRODUCT(input, w) or (w, input);  neg = SCALE(target, -1);
- *   residual = ADD(gp, neg) (either order);  loss = SQUARED_NORM(residual)
- * with `w` its only PARAMETER (no constraint) and `loss` its loss node;
- * anything else returns GEO_V8_BAD_PROGRAM. The parameter's value and Adam
- * moments are updated in place in the program (transactional), the step
- * count advances, gradients are cleared, and the INPUT/TARGET node values are
- * left unchanged. *loss_sum (may be NULL) receives sum_s 0.5 |r_s|^2.
+ * node `input_node` to inputs[s] and the TARGET node `target_node` to
+ * targets[s], geo_v8_forward, geo_v8_backward(accumulate = s != 0); then
+ * geo_v8_optimizer_step(optimizer, ..., gradient_scale)
+ * (reference src/full_cycle_v8.c:569-1041, per sample). Any compiled program:
+ *   - the graph gp = GEOMETRIC_PRODUCT(input, w) or (w, input);
+ *     neg = SCALE(target, -1); residual = ADD(gp, neg) (either order);
+ *     loss = SQUARED_NORM(residual), with `w` its only PARAMETER and no
+ *     constraint, runs as one fused streaming pass on the tensor cores;
+ *   - every other graph (all node kinds, constraints, several parameters,
+ *     STATE leaves held fixed across the batch) runs per sample on the GPU with
+ *     the reference's arithmetic, gradients summed over the batch.
+ * target_node may be GEO_V8_INVALID_NODE (device_targets then unused) for the
+ * general path. Parameters and Adam moments are updated in place
+ * (transactional), the step count advances, gradients are cleared; node
+ * values other than the parameters are left unchanged. *loss_sum (may be
+ * NULL) receives the sum over the batch of the loss node's value.
  * Synchronous; returns geo_v8_status_t values (declared in
  * geo/full_cycle_v8.h, passed here as int to keep this header independent). */
 int geo_b200_v8_batch_train_step(void *program, uint32_t input_node, uint32_t target_node,
                                  const double *device_inputs, const double *device_targets, size_t batch,
                                  int optimizer, double learning_rate, double beta1, double beta2, double epsilon,
                                  double gradient_scale, double *loss_sum);
+
+/* Batched inference: for every sample s, set `input_node` to inputs[s], run
+ * geo_v8_forward and write the value of `output_node` to outputs[s]
+ * ([batch][2^n] device arrays). Every other leaf keeps its value; node values
+ * in the program are not modified. Synchronous; geo_v8_status_t values. */
+int geo_b200_v8_batch_forward(void *program, uint32_t input_node, const double *device_inputs, size_t batch,
+                              uint32_t output_node, double *device_outputs);
 
 /* ---- 2c. parameter VJP that allocates nothing -------------------------- */
 

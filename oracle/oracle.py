@@ -380,6 +380,36 @@ class Reference:
         return np.array(params), np.array(losses)
 
 
+    def v8_composed_train(self, signature, values, xs, ts, optimizer: int, lr: float, steps: int,
+                          b1: float = 0.9, b2: float = 0.999, eps: float = 1e-8):
+        """Per-sample V8 training of the all-node-kinds graph (composed_graph):
+        every step zero_grad, then per sample set x and target, forward,
+        backward(accumulate = sample != 0), then optimizer_step(gradient_scale =
+        1/B) (reference src/full_cycle_v8.c:569-1041). Returns (w1 after each
+        step, w2 after each step, summed loss of each step)."""
+        L = self.lib
+        n = len(signature)
+        prog = (ctypes.c_uint8 * 256)()
+        ids = composed_graph(L, prog, signature, lambda c: self._mv(signature, c), values)
+        w1s, w2s, losses = [], [], []
+        try:
+            for _ in range(steps):
+                assert L.geo_v8_zero_grad(prog) == 0
+                total = 0.0
+                for j in range(xs.shape[0]):
+                    assert L.geo_v8_set_value(prog, ids["x"], ctypes.byref(self._mv(signature, xs[j]))) == 0
+                    assert L.geo_v8_set_value(prog, ids["y"], ctypes.byref(self._mv(signature, ts[j]))) == 0
+                    assert L.geo_v8_forward(prog) == 0
+                    assert L.geo_v8_backward(prog, 1 if j else 0) == 0
+                    total += ctypes.cast(L.geo_v8_value(prog, ids["loss"]), ctypes.POINTER(MvF64)).contents.coefficients[0]
+                assert L.geo_v8_optimizer_step(prog, optimizer, lr, b1, b2, eps, 1.0 / xs.shape[0]) == 0
+                for key, out in (("p1", w1s), ("p2", w2s)):
+                    out.append(self._coeffs(ctypes.cast(L.geo_v8_value(prog, ids[key]), ctypes.POINTER(MvF64)).contents, n))
+                losses.append(total)
+        finally:
+            L.geo_v8_program_free(prog)
+        return np.array(w1s), np.array(w2s), np.array(losses)
+
 def composed_graph(L, prog, signature, mv, values) -> dict:
     """Build the all-node-kinds graph of the reference test
     (tests/test_full_cycle_v8.c:158-181) through any library exposing the

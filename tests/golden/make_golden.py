@@ -94,6 +94,21 @@ def main() -> None:
             loss, g1, g2 = ref.v8_composed(sig, values)
             data[f"v8c_n{n}q{q}_loss"] = np.array([loss])
             data[f"v8c_n{n}q{q}_g1"], data[f"v8c_n{n}q{q}_g2"] = g1, g2
+    # Per-sample training of the all-node-kinds graph over a small batch (the
+    # general path of the batched V8 step is checked against these).
+    for n, q in [(2, 0), (3, 1), (4, 0), (5, 2), (6, 0), (6, 3)]:
+        sig = canonical_signature(n, q)
+        N = 1 << n
+        values = {"input": orc.v8_mv_fill(n, 3 + n + q), "target": orc.v8_mv_fill(n, 11 + 2 * n + q),
+                  "w1": orc.v8_mv_fill(n, 19 + n + q), "w2": orc.v8_mv_fill(n, 29 + n + q)}
+        xs = splitmix_uniform(91 + n + q, (9, N))
+        ts = splitmix_uniform(92 + n + q, (9, N))
+        data[f"v8cb_n{n}q{q}_x"], data[f"v8cb_n{n}q{q}_t"] = xs, ts
+        for opt in (1, 2):
+            w1s, w2s, losses = ref.v8_composed_train(sig, values, xs, ts, opt, 1e-2, steps=3)
+            data[f"v8cb_n{n}q{q}_opt{opt}_w1"] = w1s
+            data[f"v8cb_n{n}q{q}_opt{opt}_w2"] = w2s
+            data[f"v8cb_n{n}q{q}_opt{opt}_loss"] = losses
     np.savez_compressed(OUT, **data)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes, {len(data)} arrays)")
 
