@@ -30,6 +30,8 @@ import subprocess
 import sys
 import time
 
+import numpy as np
+
 METRIC = "multivector products/s and training samples/s at Cl(6,0), % of HBM/FP64 roofline"
 UNIT = "training samples/s"
 BYTES_PER_SAMPLE = 2 * 64 * 8     # read x and t once per step (float64, 64 blades)
@@ -45,7 +47,7 @@ def parse():
     p.add_argument("--batch-log2", type=int, default=22, help="per-GPU batch = 2^k (22 is the headline shape)")
     p.add_argument("--negative", type=int, default=0, help="q of Cl(6-q, q); 0 = Cl(6,0)")
     p.add_argument("--no-extras", action="store_true", help="skip e2e, Cl(3,3) and cpu_baseline legs")
-    p.add_argument("--leg", choices=["train", "pairwise-f32"], default="train",
+    p.add_argument("--leg", choices=["train", "pairwise-f32", "v8-graph"], default="train",
                    help="pairwise-f32: run only the float32 pairwise sweep (for profiling)")
     p.add_argument("--pairwise-log2", type=int, default=26, help="batch 2^k of the float32 pairwise sweep")
     p.add_argument("--algorithm", choices=["auto", "cayley", "representation"], default="auto",
@@ -292,6 +294,74 @@ def cpu_baseline_leg(negative: int) -> dict:
             "sample": f"{chunks} chunks of 1024 samples of the Cl(6,{negative}) shape (forward+VJP), {dt:.1f} s"}
 
 
+V8_GRAPH_LOG2 = 16
+# Explicitly rounded FP64 operations per sample of the all-node-kinds graph at
+# n = 6: the GP node costs 3 x 4096 forward (two multiplies and an add per
+# term) and 2 x 3 x 4096 backward; the other 12 nodes add < 2% and are ignored.
+V8_GRAPH_FP64_OPS = 9 * 4096
+
+
+def v8_graph_leg(args, world) -> dict:
+    """geo_b200_v8_batch_train_step on the all-node-kinds graph (general path), Cl(6,0), Adam."""
+    import torch
+
+    from geometricelementaryoperators_b200 import v8
+    from geometricelementaryoperators_b200.synthetic import normal
+
+    batch = 1 << V8_GRAPH_LOG2
+    sig = [1] * 6
+    prog, ids = v8.all_node_kinds_graph(sig, normal(501, (64,), 0.25), normal(502, (64,), 0.25))
+    gen = torch.Generator(device="cuda").manual_seed(503)
+    X = torch.rand((batch, 64), dtype=torch.float64, device="cuda", generator=gen).mul_(2).sub_(1)
+    T = torch.rand((batch, 64), dtype=torch.float64, device="cuda", generator=gen).mul_(2).sub_(1)
+
+    def step():
+        return prog.batch_train_step(ids["x"], ids["y"], X.data_ptr(), T.data_ptr(), batch, v8.ADAM, 1e-3)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    steps = max(3, min(args.steps, 5))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    sec = max_over_ranks((time.perf_counter() - t0) / steps, world)
+    prog.free()
+    rate = batch / sec
+    return {"workload": "all-node-kinds V8 graph (GP, tanh, sigmoid, Hadamard, reverse, involution, conjugate, "
+                        f"grade projection, normalisation, squared norm), Cl(6,0), batch 2^{V8_GRAPH_LOG2} per GPU, "
+                        "Adam, general batched path",
+            "value": rate * world, "unit": "training samples/s", "ms_per_step": sec * 1e3,
+            "timing": "host wall clock around the synchronous call, max over ranks",
+            "fp64_ops_per_s": rate * V8_GRAPH_FP64_OPS,
+            "fp64_pipe_frac": rate * V8_GRAPH_FP64_OPS / 16.8e12,
+            "fp64_pipe_peak": "16.8e12 non-fused FP64 operations/s (measured DFMA instruction rate, 33.6 TFLOP/s / 2)"}
+
+
+def v8_graph_reference_leg() -> dict:
+    """The reference's per-sample V8 loop (oracle/_ref) on the same graph, 1 core, bounded sample."""
+    from oracle import oracle as orc
+
+    if not orc.REF_SO.exists():
+        return {"value": None, "unit": "training samples/s", "cores": 1, "kind": "reference",
+                "sample": "unavailable: oracle/_ref not built"}
+    from geometricelementaryoperators_b200.synthetic import normal, splitmix_uniform
+
+    ref = orc.Reference()
+    values = {"input": np.zeros(64), "target": np.zeros(64), "w1": normal(501, (64,), 0.25),
+              "w2": normal(502, (64,), 0.25)}
+    B = 2048
+    xs = splitmix_uniform(504, (B, 64))
+    ts = splitmix_uniform(505, (B, 64))
+    t0 = time.perf_counter()
+    ref.v8_composed_train([1] * 6, values, xs, ts, 2, 1e-3, steps=1)
+    dt = time.perf_counter() - t0
+    return {"value": B / dt, "unit": "training samples/s", "cores": 1, "kind": "reference",
+            "sample": f"one Adam step over {B} samples of the same graph through the reference's per-sample "
+                      f"geo_v8_* loop, {dt:.2f} s"}
+
+
 def pairwise_f32_leg(lib, args, world) -> dict:
     """y = a * b per element, float32, Cl(6,0); a even-grade stored compact."""
     import torch
@@ -430,6 +500,7 @@ def run_b200(args, world, rank, local):
         # Float32 pairwise products, Cl(6,0), batch 2^26: even-grade left operand
         # (compact, 32 floats), dense right operand; HBM-bound sweep.
         extras["pairwise_f32"] = pairwise_f32_leg(lib, args, world)
+        extras["v8_graph"] = v8_graph_leg(args, world)
         # Same step on Cl(3,3) (the second signature of the headline config).
         X2, T2, w2 = X, T, w0
         tr33 = Trainer(lib, [1, 1, 1, -1, -1, -1], w2)
@@ -507,8 +578,11 @@ def run_b200(args, world, rank, local):
             line["cl33"] = extras["cl33"]
         if "pairwise_f32" in extras:
             line["pairwise_f32"] = extras["pairwise_f32"]
+        if "v8_graph" in extras:
+            line["v8_graph"] = extras["v8_graph"]
         if world == 1 and not args.no_extras:
             line["cpu_baseline"] = cpu_baseline_leg(q)
+            line["v8_graph"]["cpu_baseline"] = v8_graph_reference_leg()
         print(json.dumps(line), flush=True)
     tr.destroy()
     if world > 1:
@@ -526,6 +600,13 @@ def main():
         return
     world, rank, local = dist_setup(args.gpus)
     try:
+        if args.leg == "v8-graph":
+            res = v8_graph_leg(args, world)
+            if rank == 0:
+                if world == 1:
+                    res["cpu_baseline"] = v8_graph_reference_leg()
+                print(json.dumps(res), flush=True)
+            return
         if args.leg == "pairwise-f32":
             from geometricelementaryoperators_b200 import abi
 

@@ -241,3 +241,34 @@ def test_constrained_parameter_and_status_rules():
     assert np.array_equal(value(L, batched, bi["w"], n), before)
     L.geo_v8_program_free(ctypes.byref(loop))
     L.geo_v8_program_free(ctypes.byref(batched))
+
+
+def test_package_graph_builder_matches_reference_test_graph():
+    """geometricelementaryoperators_b200.v8.all_node_kinds_graph builds the reference test's graph:
+    same batched losses and one training step as the graph built node by node."""
+    import torch
+
+    from geometricelementaryoperators_b200 import v8
+
+    L = _lib()
+    n, q = 5, 1
+    sig = canonical_signature(n, q)
+    values = _values(n, q)
+    ref_prog, rids = _composed(L, sig, values)
+    prog, ids = v8.all_node_kinds_graph(sig, values["w1"], values["w2"], values["input"], values["target"])
+    B = 64
+    xs = splitmix_uniform(601, (B, 1 << n))
+    ts = splitmix_uniform(602, (B, 1 << n))
+    dx, dt = dev(xs), dev(ts)
+    a = torch.zeros((B, 1 << n), dtype=torch.float64, device="cuda")
+    b = torch.zeros_like(a)
+    prog.batch_forward(ids["x"], dx.data_ptr(), B, ids["loss"], a.data_ptr())
+    assert L.geo_b200_v8_batch_forward(ctypes.byref(ref_prog), rids["x"], ctypes.c_void_p(dx.data_ptr()), B,
+                                       rids["loss"], ctypes.c_void_p(b.data_ptr())) == 0
+    assert torch.equal(a, b)
+    loss = prog.batch_train_step(ids["x"], ids["y"], dx.data_ptr(), dt.data_ptr(), B, v8.ADAM, 1e-2)
+    st, ref_loss = _batch_step(L, ref_prog, rids["x"], rids["y"], dx, dt, B, 2)
+    assert st == 0 and loss == ref_loss
+    assert np.array_equal(prog.value(ids["w1"]), value(L, ref_prog, rids["p1"], n))
+    prog.free()
+    L.geo_v8_program_free(ctypes.byref(ref_prog))
