@@ -434,6 +434,17 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, unsigned b
                  : "memory");
 }
 
+// D(16x8) += A(16x16) * B(16x8), float64: a[i] = A[g + 8 (i % 2)][t + 4 (i / 2)],
+// b[j] = B[t + 4 j][g]; C as in mma_16x8x4.
+__device__ __forceinline__ void mma_16x8x16(double (&c)[4], const double (&a)[8], const double (&b)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5,%6,%7,%8,%9,%10,%11}, "
+        "{%12,%13,%14,%15}, {%0,%1,%2,%3};\n"
+        : "+d"(c[0]), "+d"(c[1]), "+d"(c[2]), "+d"(c[3])
+        : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(a[4]), "d"(a[5]), "d"(a[6]), "d"(a[7]), "d"(b[0]),
+          "d"(b[1]), "d"(b[2]), "d"(b[3]));
+}
+
 // D(8x8) += A(8x4) * B(4x8): a0 = A[g][t], b0 = B[t][g], c0,c1 = C[g][2t, 2t+1].
 __device__ __forceinline__ void mma_8x8x4(double (&c)[2], double a0, double b0) {
     asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};\n"
@@ -588,11 +599,13 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
         const int cw = warp - kWsProducers / 32;
         const int g = lane >> 2, t4 = lane & 3;
         constexpr int KT = D / 4;
-        double wa0[KT], wa1[KT];
+        // W'^T as the A operand: D = 16 one m16n8k16 fragment, wa[i] = W'[t + 4 (i / 2)][g + 8 (i % 2)];
+        // D = 8 the m8n8k4 fragments wa[kk] = W'[4 kk + t][g].
+        double wa[8];
 #pragma unroll
-        for (int kk = 0; kk < KT; ++kk) {
-            wa0[kk] = Wp[(4 * kk + t4) * D + g];
-            wa1[kk] = D == 16 ? Wp[(4 * kk + t4) * D + g + 8] : 0.0;
+        for (int i = 0; i < 8; ++i) {
+            if (D == 16) wa[i] = Wp[(t4 + 4 * (i / 2)) * D + g + 8 * (i % 2)];
+            else wa[i] = i < KT ? Wp[(4 * i + t4) * D + g] : 0.0;
         }
         for (int k = 0; k < K; ++k) {
             const int st = k % kWsStages;
@@ -605,29 +618,34 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
                 n0[0] = (cw * G::GPW + j) * 8;
                 n0[1] = n0[0] + 8;
                 if constexpr (D == 16) {
+                    // GEMM 1 per row group: one m16n8k16 (M = output column j, N = 8 rows, K = 16).
                     double c[2][4];
 #pragma unroll
-                    for (int q = 0; q < 2; ++q) c[q][0] = c[q][1] = c[q][2] = c[q][3] = 0.0;
+                    for (int q = 0; q < 2; ++q) {
+                        double b[4];
 #pragma unroll
-                    for (int kk = 0; kk < KT; ++kk)
+                        for (int kk = 0; kk < 4; ++kk) b[kk] = xs[ws_index<D>(n0[q] + g, 4 * kk + t4)];
+                        c[q][0] = c[q][1] = c[q][2] = c[q][3] = 0.0;
+                        mma_16x8x16(c[q], wa, b);
+                    }
+                    // Epilogue in registers; GEMM 2 over both row groups as one m16n8k16 per
+                    // 8-column tile of G', k slot t + 4 j <-> row n0[j / 2] + 2 t + j % 2.
+                    double ax[8], rlo[4], rhi[4];
 #pragma unroll
-                        for (int q = 0; q < 2; ++q)
-                            mma_16x8x4(c[q], wa0[kk], wa1[kk], xs[ws_index<D>(n0[q] + g, 4 * kk + t4)]);
-#pragma unroll
-                    for (int q = 0; q < 2; ++q)
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int row = n0[q] + 2 * t4 + h;
-                            const int plo = ws_index<D>(row, g), phi = ws_index<D>(row, g + 8);
-                            const double rlo = c[q][h] - ts[plo];
-                            const double rhi = c[q][2 + h] - ts[phi];
-                            sq = fma(rlo, rlo, sq);
-                            sq = fma(rhi, rhi, sq);
-                            worst_exp = max(worst_exp, max(exponent_bits(rlo), exponent_bits(rhi)));
-                            const double alo = xs[plo], ahi = xs[phi];
-                            mma_16x8x4(gacc[0][h], alo, ahi, rlo);
-                            mma_16x8x4(gacc[PT - 1][h], alo, ahi, rhi);
-                        }
+                    for (int j = 0; j < 4; ++j) {
+                        const int q = j >> 1, h = j & 1;
+                        const int row = n0[q] + 2 * t4 + h;
+                        const int plo = ws_index<D>(row, g), phi = ws_index<D>(row, g + 8);
+                        rlo[j] = c[q][h] - ts[plo];
+                        rhi[j] = c[q][2 + h] - ts[phi];
+                        sq = fma(rlo[j], rlo[j], sq);
+                        sq = fma(rhi[j], rhi[j], sq);
+                        worst_exp = max(worst_exp, max(exponent_bits(rlo[j]), exponent_bits(rhi[j])));
+                        ax[2 * j] = xs[plo];
+                        ax[2 * j + 1] = xs[phi];
+                    }
+                    mma_16x8x16(gacc[0][0], ax, rlo);
+                    mma_16x8x16(gacc[PT - 1][0], ax, rhi);
                 } else {
                     double c[2][2];
 #pragma unroll
@@ -635,7 +653,7 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
 #pragma unroll
                     for (int kk = 0; kk < KT; ++kk)
 #pragma unroll
-                        for (int q = 0; q < 2; ++q) mma_8x8x4(c[q], wa0[kk], xs[ws_index<D>(n0[q] + g, 4 * kk + t4)]);
+                        for (int q = 0; q < 2; ++q) mma_8x8x4(c[q], wa[kk], xs[ws_index<D>(n0[q] + g, 4 * kk + t4)]);
 #pragma unroll
                     for (int q = 0; q < 2; ++q)
 #pragma unroll
