@@ -386,8 +386,9 @@ cudaError_t launch_rep_impl(const RepDevice &rep, const double *X, const double 
 // on the previous tile meanwhile:
 //   GEMM 1 transposed, Y'^T = W'^T X'^T (W'^T fragments resident as the A
 //     operand), so each lane's accumulators hold Y'[n0 + 2t + h][g (+8)];
-//   R' = Y' - T' in registers: exactly the B fragment of GEMM 2 when the four
-//     k slots of an mma are the rows n0 + 2t + h (h = 0, 1);
+//   the accumulators start at -T' (the producers write T' negated), so GEMM 1
+//     leaves R' = Y' - T' in registers: exactly the B fragment of GEMM 2 when
+//     the k slots of an mma are the rows n0 + 2t + h;
 //   GEMM 2, G' += X'^T R', with X'^T loaded as the A operand.
 // Named barriers hand stages over (FULL: gathered, EMPTY: consumed); every
 // wait on an mbarrier is bounded and a wait that gives up marks the record as
@@ -589,7 +590,7 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
 #pragma unroll
                 for (int f = 0; f < S; ++f) {
                     xs[G::SLOTS * i * N + woff[f]] = flip_sign(vx[i][f], out_sign[f]);
-                    ts[G::SLOTS * i * N + woff[f]] = flip_sign(vt[i][f], out_sign[f]);
+                    ts[G::SLOTS * i * N + woff[f]] = flip_sign(vt[i][f], out_sign[f] ^ 0x80000000u);  // -T
                 }
             }
             named_arrive(kBarFull + st, kWsThreads);
@@ -625,7 +626,12 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
                         double b[4];
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk) b[kk] = xs[ws_index<D>(n0[q] + g, 4 * kk + t4)];
-                        c[q][0] = c[q][1] = c[q][2] = c[q][3] = 0.0;
+                        // accumulate onto -T': the result is R' = Y' - T'
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            c[q][h] = ts[ws_index<D>(n0[q] + 2 * t4 + h, g)];
+                            c[q][2 + h] = ts[ws_index<D>(n0[q] + 2 * t4 + h, g + 8)];
+                        }
                         mma_16x8x16(c[q], wa, b);
                     }
                     // Epilogue in registers; GEMM 2 over both row groups as one m16n8k16 per
@@ -636,8 +642,8 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
                         const int q = j >> 1, h = j & 1;
                         const int row = n0[q] + 2 * t4 + h;
                         const int plo = ws_index<D>(row, g), phi = ws_index<D>(row, g + 8);
-                        rlo[j] = c[q][h] - ts[plo];
-                        rhi[j] = c[q][2 + h] - ts[phi];
+                        rlo[j] = c[q][h];
+                        rhi[j] = c[q][2 + h];
                         sq = fma(rlo[j], rlo[j], sq);
                         sq = fma(rhi[j], rhi[j], sq);
                         worst_exp = max(worst_exp, max(exponent_bits(rlo[j]), exponent_bits(rhi[j])));
@@ -647,9 +653,11 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
                     mma_16x8x16(gacc[0][0], ax, rlo);
                     mma_16x8x16(gacc[PT - 1][0], ax, rhi);
                 } else {
-                    double c[2][2];
+                    double c[2][2];  // start at -T' (R' = Y' - T' after GEMM 1)
 #pragma unroll
-                    for (int q = 0; q < 2; ++q) c[q][0] = c[q][1] = 0.0;
+                    for (int q = 0; q < 2; ++q)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) c[q][h] = ts[ws_index<D>(n0[q] + 2 * t4 + h, g)];
 #pragma unroll
                     for (int kk = 0; kk < KT; ++kk)
 #pragma unroll
@@ -660,7 +668,7 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
                         for (int h = 0; h < 2; ++h) {
                             const int row = n0[q] + 2 * t4 + h;
                             const int pos = ws_index<D>(row, g);
-                            const double r = c[q][h] - ts[pos];
+                            const double r = c[q][h];
                             sq = fma(r, r, sq);
                             worst_exp = max(worst_exp, exponent_bits(r));
                             mma_8x8x4(gacc[0][h], xs[pos], r);
