@@ -21,6 +21,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = ROOT / "_build" / "geo_b200"
 LIB = PKG / "libgeo_b200.so"
+CLI = PKG / "geo_cycle_b200"  # the geo_cycle command line on the library
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -79,6 +80,15 @@ def build(verbose: bool = False, force: bool = False, extra_flags: list[str] | N
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
+    cli_src = CSRC / "cli" / "geo_cycle_main.cpp"
+    if force or not CLI.exists() or CLI.stat().st_mtime < max(LIB.stat().st_mtime, cli_src.stat().st_mtime):
+        cmd = [nvcc(), "-std=c++17", "-O2", "-I", str(ROOT / "include"), "-x", "c++", str(cli_src), "-o", str(CLI),
+               "-L", str(LIB.parent), "-lgeo_b200", "-Xlinker", "-rpath", "-Xlinker", "$ORIGIN"]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"geo_cycle_b200 link failed:\n{res.stdout}\n{res.stderr}")
     return LIB
 
 

@@ -89,11 +89,13 @@ int general_step(geo_v8_program_t *p, uint32_t input_node, uint32_t target_node,
     (void)geo_v8_zero_grad(p);
     double loss = 0.0;
     std::vector<double> grads;
-    const geo_v8_status_t st = geo::v8::run_batch(p, input_node, target_node, GEO_V8_INVALID_NODE, device_inputs,
-                                                  target_node != GEO_V8_INVALID_NODE ? device_targets : nullptr,
-                                                  nullptr, batch, 1, &loss, &grads);
-    if (st != GEO_V8_OK) return st;
     const size_t blades = (size_t)1 << p->dimension;
+    std::vector<geo::v8::RowLeaf> leaves{{input_node, 1, 0}};
+    if (target_node != GEO_V8_INVALID_NODE) leaves.push_back({target_node, 2, 0});
+    const geo_v8_status_t st =
+        geo::v8::run_batch(p, leaves, {device_inputs, blades}, {device_targets, blades}, GEO_V8_INVALID_NODE,
+                           nullptr, batch, 1, &loss, &grads);
+    if (st != GEO_V8_OK) return st;
     for (geo_v8_node_id_t i = 0; i < p->node_count; ++i)
         if (geo::v8::leaf_kind(p->nodes[i].kind) && p->nodes[i].requires_grad)
             memcpy(p->nodes[i].gradient.coefficients, &grads[(size_t)i * 64], blades * sizeof(double));
@@ -114,7 +116,8 @@ extern "C" int geo_b200_v8_batch_forward(void *program_ptr, uint32_t input_node,
     if (!p->compiled) return GEO_V8_NOT_COMPILED;
     if (device_inputs == nullptr || device_outputs == nullptr || batch == 0) return GEO_V8_INVALID_ARGUMENT;
     if (!is_kind(p, input_node, GEO_V8_NODE_INPUT) || output_node >= p->node_count) return GEO_V8_BAD_PROGRAM;
-    return geo::v8::run_batch(p, input_node, GEO_V8_INVALID_NODE, output_node, device_inputs, nullptr,
+    const size_t blades = (size_t)1 << p->dimension;
+    return geo::v8::run_batch(p, {{input_node, 1, 0}}, {device_inputs, blades}, {nullptr, 0}, output_node,
                               device_outputs, batch, 0, nullptr, nullptr);
 }
 

@@ -33,20 +33,23 @@ struct BatchNode {
     double scalar;
     int32_t requires_grad;
     int32_t grad_slot;  // >= 0 for leaves whose gradient is accumulated
+    int32_t source;     // 0: the leaf's own value; 1 / 2: row s of row source a / b
+    int32_t column;     // first column of the leaf's coefficients in that row
 };
 
 struct BatchArgs {
     const BatchNode *nodes;
     const double *leaf_values;  // [count][64]: values of the leaves that do not vary per sample
-    const double *inputs;       // [batch][blades]
-    const double *targets;      // [batch][blades] or null
+    const double *rows_a;       // per-sample rows, row s at rows_a + s * stride_a
+    const double *rows_b;
+    size_t stride_a, stride_b;
     double *outputs;            // forward-only: [batch][blades] of output_node
     double *scratch;            // [warps][2][count][64]: values, cotangents
     double *partials;           // [warps][grad_slots + 1][64]; row grad_slots holds the loss at [0]
     int *status;                // first failure (geo_v8_status_t), 0 while none
     int *failed_node;
     size_t batch;
-    int count, blades, input_node, target_node, loss_node, output_node, grad_slots, backward;
+    int count, blades, loss_node, output_node, grad_slots, backward;
     uint64_t neg[64];  // bit r of neg[l]: e_l e_r = -e_(l^r)
 };
 
@@ -102,13 +105,13 @@ __global__ void __launch_bounds__(kBatchThreads) batch_kernel(const BatchArgs a)
             double *v = vals + (size_t)i * 64;
             const int k = nd.kind;
             if (k >= GEO_V8_NODE_INPUT && k <= GEO_V8_NODE_STATE) {
-                const double *src = i == a.input_node   ? a.inputs + s * N
-                                    : i == a.target_node ? a.targets + s * N
-                                                         : a.leaf_values + (size_t)i * 64;
+                const double *src = nd.source == 1   ? a.rows_a + s * a.stride_a + nd.column
+                                    : nd.source == 2 ? a.rows_b + s * a.stride_b + nd.column
+                                                     : a.leaf_values + (size_t)i * 64;
                 const double x0 = l0 ? src[b0] : 0.0, x1 = l1 ? src[b1] : 0.0;
                 if (warp_any(!isfinite(x0) || !isfinite(x1))) {
                     // per-sample rows go through geo_v8_set_value in the reference, which rejects them
-                    fail = (i == a.input_node || i == a.target_node) ? GEO_V8_INVALID_ARGUMENT : GEO_V8_NUMERIC_FAILURE;
+                    fail = nd.source != 0 ? GEO_V8_INVALID_ARGUMENT : GEO_V8_NUMERIC_FAILURE;
                     fnode = i;
                     break;
                 }
@@ -386,9 +389,9 @@ Workspace g_batch_ws[64];
 
 }  // namespace
 
-geo_v8_status_t run_batch(geo_v8_program_t *p, uint32_t input_node, uint32_t target_node, uint32_t output_node,
-                          const double *device_inputs, const double *device_targets, double *device_outputs,
-                          size_t batch, int backward, double *loss_sum, std::vector<double> *gradients) {
+geo_v8_status_t run_batch(geo_v8_program_t *p, const std::vector<RowLeaf> &row_leaves, const RowSource &a_rows,
+                          const RowSource &b_rows, uint32_t output_node, double *device_outputs, size_t batch,
+                          int backward, double *loss_sum, std::vector<double> *gradients) {
     const int count = (int)p->node_count;
     const int blades = 1 << p->dimension;
     std::vector<BatchNode> nodes((size_t)count);
@@ -404,8 +407,20 @@ geo_v8_status_t run_batch(geo_v8_program_t *p, uint32_t input_node, uint32_t tar
         b.scalar = n.scalar;
         b.requires_grad = n.requires_grad;
         b.grad_slot = -1;
+        b.source = 0;
+        b.column = 0;
+    }
+    for (const RowLeaf &r : row_leaves) {
+        if (r.node >= (uint32_t)count || !leaf_kind(p->nodes[r.node].kind) || (r.source != 1 && r.source != 2))
+            return GEO_V8_BAD_PROGRAM;
+        nodes[r.node].source = r.source;
+        nodes[r.node].column = (int32_t)r.column;
+    }
+    for (int i = 0; i < count; ++i) {
+        const geo_v8_node_t &n = p->nodes[i];
+        BatchNode &b = nodes[(size_t)i];
         if (leaf_kind(n.kind)) {
-            if ((uint32_t)i != input_node && (uint32_t)i != target_node) {
+            if (b.source == 0) {
                 if (!mv_valid(&n.value, p->dimension, p->signature)) return GEO_V8_NUMERIC_FAILURE;
                 memcpy(&leaf_values[(size_t)i * 64], n.value.coefficients, 64 * sizeof(double));
             }
@@ -462,14 +477,14 @@ geo_v8_status_t run_batch(geo_v8_program_t *p, uint32_t input_node, uint32_t tar
     int *flags = (int *)take(256);
     a.status = flags;
     a.failed_node = flags + 1;
-    a.inputs = device_inputs;
-    a.targets = device_targets;
+    a.rows_a = a_rows.base;
+    a.stride_a = a_rows.stride;
+    a.rows_b = b_rows.base;
+    a.stride_b = b_rows.stride;
     a.outputs = device_outputs;
     a.batch = batch;
     a.count = count;
     a.blades = blades;
-    a.input_node = (int)input_node;
-    a.target_node = target_node == GEO_V8_INVALID_NODE ? -1 : (int)target_node;
     a.loss_node = (int)p->loss_node;
     a.output_node = output_node == GEO_V8_INVALID_NODE ? -1 : (int)output_node;
     a.grad_slots = slots;

@@ -50,16 +50,26 @@ geo_v8_status_t run_optimizer(geo_v8_program_t *program, int optimizer, double l
                               double beta2, double epsilon, double gradient_scale, double bias1, double bias2);
 
 // Batched execution of a compiled program over device-resident rows
-// (v8_batch.cu). input_node (and target_node, unless GEO_V8_INVALID_NODE) take
-// row s of device_inputs / device_targets for sample s; every other leaf keeps
+// (v8_batch.cu). Each RowLeaf takes, for sample s, its coefficients from row s
+// of row source 1 (a) or 2 (b), starting at `column`; every other leaf keeps
 // its value. backward != 0: per-sample forward + backward, *loss_sum = sum of
 // the loss node over the batch, (*gradients)[i * 64 + b] = gradient of leaf i
 // summed over the batch. backward == 0: forward only, row s of device_outputs
-// receives output_node's value. Synchronous; returns the first failure.
-geo_v8_status_t run_batch(geo_v8_program_t *program, uint32_t input_node, uint32_t target_node,
-                          uint32_t output_node, const double *device_inputs, const double *device_targets,
-                          double *device_outputs, size_t batch, int backward, double *loss_sum,
-                          std::vector<double> *gradients);
+// ([batch][2^n]) receives output_node's value. Synchronous; returns the first
+// failure (a non-finite row value gives GEO_V8_INVALID_ARGUMENT, as
+// geo_v8_set_value would).
+struct RowLeaf {
+    uint32_t node;
+    int source;
+    size_t column;
+};
+struct RowSource {
+    const double *base;
+    size_t stride;  // doubles per row
+};
+geo_v8_status_t run_batch(geo_v8_program_t *program, const std::vector<RowLeaf> &row_leaves, const RowSource &a,
+                          const RowSource &b, uint32_t output_node, double *device_outputs, size_t batch,
+                          int backward, double *loss_sum, std::vector<double> *gradients);
 
 }  // namespace v8
 }  // namespace geo

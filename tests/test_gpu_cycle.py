@@ -1,0 +1,143 @@
+"""The geo_cycle runner on the GPU (geo_cycle_b200, geo/geo_cycle_b200.h)
+against the reference's own runner: checkpoints after training, predictions,
+exported headers and PASS lines for the fixture models of
+tests/golden/cycle (made by tests/golden/make_cycle_golden.py), byte-identical
+resume, and the reference's handling of bad inputs."""
+from __future__ import annotations
+
+import pathlib
+import shutil
+import subprocess
+
+import numpy as np
+import pytest
+
+from tests.conftest import max_violation, tol_close
+
+pytestmark = pytest.mark.gpu
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+CYCLE = ROOT / "tests" / "golden" / "cycle"
+RUNNER = ROOT / "geometricelementaryoperators_b200" / "geo_cycle_b200"
+MODELS = ["gp_exact", "mlp", "all_ops", "constraint", "recurrent", "resume1", "resume2"]
+# Adam divides each update by the root of its second moment, which amplifies the
+# ulp-level differences of the device tanh/exp and of the order of the sum over
+# a minibatch on gradient components that nearly cancel (see test_gpu_v8_batch).
+TOL = {"gp_exact": 1e-12, "recurrent": 1e-12}
+ADAM_TOL = 1e-10
+
+
+def run(*args, ok=True):
+    res = subprocess.run([str(RUNNER), *map(str, args)], capture_output=True, text=True, timeout=600)
+    if ok:
+        assert res.returncode == 0, res.stderr
+    return res
+
+
+def base(name):
+    return "resume" if name.startswith("resume") else name
+
+
+def checkpoint(path):
+    """{'step': n, 'parameter:<name>': {...}, 'state:<name>': [...]} from a checkpoint file."""
+    out, cur = {}, None
+    for line in pathlib.Path(path).read_text().splitlines():
+        key, _, value = line.partition("=")
+        if key == "optimizer_step":
+            out["step"] = int(value)
+        elif key == "parameter":
+            name, constraint = value.split(",")
+            cur = out[f"parameter:{name}"] = {"constraint": int(constraint)}
+        elif key == "state":
+            cur = out[f"state:{value}"] = {}
+        elif key in ("value", "first", "second"):
+            cur[key] = np.array([float(v) for v in value.split(",")])
+    return out
+
+
+def pass_fields(line):
+    return dict(f.split("=", 1) for f in line.split()[2:])
+
+
+@pytest.fixture(scope="module")
+def runner():
+    if not RUNNER.exists():
+        pytest.fail("geo_cycle_b200 is not built (run __graft_entry__.build())")
+    return RUNNER
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_train_matches_reference(runner, name, tmp_path):
+    ckpt = tmp_path / f"{name}.checkpoint"
+    res = run("train", CYCLE / f"{name}.geoir", CYCLE / f"{base(name)}.csv", ckpt)
+    ours, ref = pass_fields(res.stdout.strip()), pass_fields((CYCLE / f"{name}.train.txt").read_text().strip())
+    for key in ("epochs", "rows", "batch_size", "parameters", "states"):
+        assert ours[key] == ref[key], key
+    tol = TOL.get(name, ADAM_TOL)
+    for key in ("initial_loss", "final_loss"):
+        assert tol_close(float(ours[key]), float(ref[key]), tol), (key, ours[key], ref[key])
+    got, want = checkpoint(ckpt), checkpoint(CYCLE / f"{name}.checkpoint")
+    assert got.keys() == want.keys() and got["step"] == want["step"]
+    for key in want:
+        if key == "step":
+            continue
+        for part in want[key]:
+            if part == "constraint":
+                assert got[key][part] == want[key][part]
+                continue
+            assert tol_close(got[key][part], want[key][part], tol), (key, part, max_violation(got[key][part],
+                                                                                              want[key][part], tol))
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_predict_and_export_from_reference_checkpoint(runner, name, tmp_path):
+    """Given the reference's checkpoint, predictions match to 1e-12 and the C header is byte-identical."""
+    out = tmp_path / "pred.csv"
+    res = run("predict", CYCLE / f"{name}.geoir", CYCLE / f"{name}.checkpoint", CYCLE / f"{base(name)}.predict_in.csv",
+              out)
+    assert res.stdout.startswith("GEO_CYCLE_PREDICT: PASS rows=6 ")
+    got = np.loadtxt(out, delimiter=",", ndmin=2)
+    want = np.loadtxt(CYCLE / f"{name}.predict.csv", delimiter=",", ndmin=2)
+    assert tol_close(got, want, 1e-12), max_violation(got, want, 1e-12)
+    header = tmp_path / f"{name}.h"
+    res = run("export-c", CYCLE / f"{name}.geoir", CYCLE / f"{name}.checkpoint", header, name)
+    assert header.read_bytes() == (CYCLE / f"{name}.h").read_bytes()
+    res = run("check", CYCLE / f"{name}.geoir")
+    assert res.stdout == (CYCLE / f"{name}.check.txt").read_text()
+
+
+def test_resume_is_byte_identical(runner, tmp_path):
+    """Two epochs in one run == one epoch, a checkpoint, and one more epoch resumed from it."""
+    data = CYCLE / "resume.csv"
+    run("train", CYCLE / "resume2.geoir", data, tmp_path / "fresh")
+    run("train", CYCLE / "resume1.geoir", data, tmp_path / "half")
+    run("train", CYCLE / "resume1.geoir", data, tmp_path / "resumed", tmp_path / "half")
+    assert (tmp_path / "resumed").read_bytes() == (tmp_path / "fresh").read_bytes()
+
+
+def test_bad_inputs_fail_like_the_reference(runner, tmp_path):
+    ir = CYCLE / "mlp.geoir"
+    rows = (CYCLE / "mlp.csv").read_text().splitlines()
+    cases = {
+        "nan_row": rows[:3] + [rows[3].replace(rows[3].split(",")[2], "nan", 1)] + rows[4:],
+        "short_row": rows[:5] + [",".join(rows[5].split(",")[:-1])] + rows[6:],
+        "text_row": rows[:2] + ["1,2,three"] + rows[3:],
+        "empty": ["# only a comment"],
+    }
+    for label, lines in cases.items():
+        data = tmp_path / f"{label}.csv"
+        data.write_text("\n".join(lines) + "\n")
+        res = run("train", ir, data, tmp_path / "ckpt", ok=False)
+        assert res.returncode == 1, label
+        assert res.stderr == "geo_cycle: invalid training data or runtime failure\n", label
+        assert not (tmp_path / "ckpt").exists()
+    res = run("train", ir, tmp_path / "missing.csv", tmp_path / "ckpt", ok=False)
+    assert res.returncode == 1 and res.stderr == ""
+    # a checkpoint of another model is rejected
+    shutil.copy(CYCLE / "gp_exact.checkpoint", tmp_path / "other")
+    res = run("predict", ir, tmp_path / "other", CYCLE / "resume.predict_in.csv", tmp_path / "p.csv", ok=False)
+    assert res.returncode == 1 and "invalid or mismatched checkpoint" in res.stderr
+    bad_ir = tmp_path / "bad.geoir"
+    bad_ir.write_text((CYCLE / "mlp.geoir").read_text().replace("geo_model_ir=8", "geo_model_ir=7"))
+    res = run("check", bad_ir, ok=False)
+    assert res.returncode == 1 and res.stderr == f"geo_cycle: invalid model IR '{bad_ir}'\n"
