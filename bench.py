@@ -232,6 +232,17 @@ def reference_step(pool, workers, chunks, signature):
     return done, time.perf_counter() - t0
 
 
+def headline_config(args, world) -> dict:
+    """The workload both arms report (the reference arm times bounded samples of it)."""
+    q = args.negative
+    batch = 1 << args.batch_log2
+    return {"workload": f"Cl({6 - q},{q}) full-cycle training step (forward + parameter VJP + MSE + Adam), "
+                        f"parameter on the right, float64, batch 2^{args.batch_log2} per GPU",
+            "batch_per_gpu": batch, "global_batch": batch * world, "blades": 64,
+            "signature": [1] * (6 - q) + [-1] * q, "optimizer": "adam lr=1e-3 b=(0.9,0.999) eps=1e-8",
+            "l2": "inputs 4 GiB per GPU per step > 126 MB L2; no flush needed", "parallelism": f"dp{world}"}
+
+
 def run_reference_arm(args, world, rank):
     """The reference's own CPU implementation on all host threads (rank 0 only)."""
     if rank != 0:
@@ -261,13 +272,13 @@ def run_reference_arm(args, world, rank):
             total += done
             elapsed += dt
     value = total / elapsed
-    sample = f"{workers} processes x {chunks} chunks of 1024 samples per step (forward+VJP; Adam is O(64))"
+    sample = (f"each step: {workers} processes x {chunks} chunks of 1024 samples of this workload through the "
+              "reference's batch_gp forward and parameter VJP (the Adam update is O(64) per step)")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * elapsed / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": f"Cl({6 - args.negative},{args.negative}) full-cycle training step, float64, "
-                               "reference CPU batch_gp forward+VJP on 1024-sample chunks", "blades": 64},
+        "config": headline_config(args, world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": workers, "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -558,12 +569,7 @@ def run_b200(args, world, rank, local):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": f"Cl({6 - q},{q}) full-cycle training step (forward + parameter VJP + MSE + "
-                                   "Adam), parameter on the right, float64, batch 2^%d per GPU" % args.batch_log2,
-                       "batch_per_gpu": batch, "global_batch": batch * world, "blades": 64,
-                       "signature": sig, "optimizer": "adam lr=1e-3 b=(0.9,0.999) eps=1e-8",
-                       "l2": "inputs 4 GiB per GPU per step > 126 MB L2; no flush needed",
-                       "parallelism": f"dp{world}"},
+            "config": headline_config(args, world),
             "roofline": roofline,
             "gpu_launches": args.steps * 3,
             "clocks": clock_info,
