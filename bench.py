@@ -25,6 +25,7 @@ import ctypes
 import json
 import math
 import os
+import shutil
 import statistics
 import subprocess
 import sys
@@ -302,7 +303,37 @@ def cpu_baseline_leg(negative: int) -> dict:
         chunks += 1
     dt = time.perf_counter() - t0
     return {"value": done / dt, "unit": UNIT, "cores": 1, "kind": kind,
-            "sample": f"{chunks} chunks of 1024 samples of the Cl(6,{negative}) shape (forward+VJP), {dt:.1f} s"}
+            "sample": f"{chunks} chunks of 1024 samples of the Cl(6,{negative}) shape (forward+VJP), {dt:.1f} s",
+            "reference_benchmarks": reference_benchmarks()}
+
+
+def reference_benchmarks() -> dict:
+    """The reference's own CPU benchmarks, unmodified (oracle/_ref), pinned to one core:
+    samples/s at n = 6 for each batch size of their built-in matrix."""
+    import tempfile
+
+    out = {}
+    ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "oracle", "_ref")
+    with tempfile.TemporaryDirectory() as tmp:
+        for name, backend in (("bench_v8_batch_gp", "geo_v8_batch"), ("bench_v8_full_cycle", "geo_v8")):
+            exe = os.path.join(ref, name)
+            csv_path = os.path.join(tmp, name + ".csv")
+            if not os.path.exists(exe):
+                out[name] = "unavailable: not built"
+                continue
+            cmd = ([] if shutil.which("taskset") is None else ["taskset", "-c", "0"]) + [exe, csv_path]
+            res = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
+            if res.returncode != 0 or not os.path.exists(csv_path):
+                out[name] = f"failed with exit code {res.returncode}"
+                continue
+            rows = {}
+            with open(csv_path) as f:
+                for line in f.read().splitlines()[1:]:
+                    b, mode, n, batch, rate, _ = line.split(",")
+                    if b == backend and n == "6":
+                        rows[f"n6_{mode}_batch{batch}"] = float(rate)
+            out[name] = {"unit": "samples/s", "cores": 1, **rows}
+    return out
 
 
 V8_GRAPH_LOG2 = 16

@@ -27,6 +27,7 @@ namespace v8 {
 namespace {
 
 constexpr int kBatchThreads = 256;
+constexpr int kBatchCtasPerSm = 2;  // 16 warps per SM hide the latency of the per-sample chains
 
 struct BatchNode {
     int32_t kind, left, right, grade;
@@ -35,6 +36,8 @@ struct BatchNode {
     int32_t grad_slot;  // >= 0 for leaves whose gradient is accumulated
     int32_t source;     // 0: the leaf's own value; 1 / 2: row s of row source a / b
     int32_t column;     // first column of the leaf's coefficients in that row
+    int32_t invariant;  // the value does not depend on the per-sample rows
+    int32_t reserved;
 };
 
 struct BatchArgs {
@@ -66,6 +69,40 @@ __device__ __forceinline__ int map_sign(int mode, int blade) {
 }
 __device__ __forceinline__ bool warp_any(bool v) { return __any_sync(0xffffffffu, v); }
 
+// A multivector held by a warp as (lo, hi): lane l has blades l and l + 32.
+// Blade q, on every lane:
+__device__ __forceinline__ double blade_at(double lo, double hi, int q) {
+    return __shfl_sync(0xffffffffu, q < 32 ? lo : hi, q & 31);
+}
+// Blade lane ^ q (first blade of the lane) and (lane + 32) ^ q (second):
+__device__ __forceinline__ double xor_first(double lo, double hi, int q) {
+    return __shfl_xor_sync(0xffffffffu, q < 32 ? lo : hi, q & 31);
+}
+__device__ __forceinline__ double xor_second(double lo, double hi, int q) {
+    return __shfl_xor_sync(0xffffffffu, q < 32 ? hi : lo, q & 31);
+}
+// Sequential sums over the blades in blade order (the reference's loops), on
+// every lane; operands come from registers, so only the adds form a chain.
+__device__ __forceinline__ double blade_dot(double x0, double x1, double y0, double y1, int N) {
+    double acc = 0.0;
+#pragma unroll 8
+    for (int q = 0; q < 64; ++q) {
+        if (q >= N) break;
+        acc = add(acc, mul(blade_at(x0, x1, q), blade_at(y0, y1, q)));
+    }
+    return acc;
+}
+__device__ __forceinline__ double half_squared_norm(double x0, double x1, int N) {
+    double acc = 0.0;
+#pragma unroll 8
+    for (int q = 0; q < 64; ++q) {
+        if (q >= N) break;
+        const double v = blade_at(x0, x1, q);
+        acc = add(acc, mul(mul(0.5, v), v));
+    }
+    return acc;
+}
+
 __device__ void record_failure(const BatchArgs &a, int status, int node) {
     if ((threadIdx.x & 31) == 0 && atomicCAS(a.status, 0, status) == 0) *a.failed_node = node;
 }
@@ -83,7 +120,7 @@ __device__ bool accumulate2(const BatchArgs &a, double *dest, double s0, double 
     return true;
 }
 
-__global__ void __launch_bounds__(kBatchThreads) batch_kernel(const BatchArgs a) {
+__global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(const BatchArgs a) {
     const int lane = threadIdx.x & 31;
     const size_t warp = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const size_t warps = ((size_t)gridDim.x * blockDim.x) >> 5;
@@ -102,6 +139,9 @@ __global__ void __launch_bounds__(kBatchThreads) batch_kernel(const BatchArgs a)
         int fail = 0, fnode = -1;
         for (int i = 0; i < C && !fail; ++i) {
             const BatchNode nd = a.nodes[i];
+            // A value that no per-sample row reaches is computed for the warp's
+            // first sample and stays in its scratch for the others.
+            if (nd.invariant && s != warp) continue;
             double *v = vals + (size_t)i * 64;
             const int k = nd.kind;
             if (k >= GEO_V8_NODE_INPUT && k <= GEO_V8_NODE_STATE) {
@@ -128,12 +168,16 @@ __global__ void __launch_bounds__(kBatchThreads) batch_kernel(const BatchArgs a)
                 case GEO_V8_NODE_SCALE: o0 = mul(L[b0], nd.scalar); o1 = mul(L[b1], nd.scalar); break;
                 case GEO_V8_NODE_GEOMETRIC_PRODUCT: {
                     // reference src/operator_kernel.c:412-447: left-blade-major, zero left coefficients skipped
+                    const double L0 = L[b0], L1 = L[b1], R0 = R[b0], R1 = R[b1];
                     double c0 = 0.0, c1 = 0.0;
-                    for (int l = 0; l < N; ++l) {
-                        const double lv = L[l];
+#pragma unroll 8
+                    for (int l = 0; l < 64; ++l) {
+                        if (l >= N) break;
+                        const double lv = blade_at(L0, L1, l);
+                        const double r0 = xor_first(R0, R1, l), r1 = xor_second(R0, R1, l);
                         if (lv == 0.0) continue;
-                        if (l0) c0 = add(c0, mul(mul(lv, R[l ^ b0]), gsign(a, l, l ^ b0)));
-                        if (l1) c1 = add(c1, mul(mul(lv, R[l ^ b1]), gsign(a, l, l ^ b1)));
+                        if (l0) c0 = add(c0, mul(mul(lv, r0), gsign(a, l, l ^ b0)));
+                        if (l1) c1 = add(c1, mul(mul(lv, r1), gsign(a, l, l ^ b1)));
                     }
                     o0 = c0;
                     o1 = c1;
@@ -161,10 +205,7 @@ __global__ void __launch_bounds__(kBatchThreads) batch_kernel(const BatchArgs a)
                     break;
                 }
                 case GEO_V8_NODE_EUCLIDEAN_NORMALIZE: {
-                    double n2 = 0.0;
-                    if (lane == 0)
-                        for (int q = 0; q < N; ++q) n2 = add(n2, mul(L[q], L[q]));
-                    n2 = __shfl_sync(0xffffffffu, n2, 0);
+                    const double n2 = blade_dot(L[b0], L[b1], L[b0], L[b1], N);
                     const double floor_value = nd.scalar > 0.0 ? nd.scalar : 1e-12;
                     if (!isfinite(n2) || n2 <= mul(floor_value, floor_value)) { fail = GEO_V8_NUMERIC_FAILURE; fnode = i; break; }
                     const double inverse = __ddiv_rn(1.0, __dsqrt_rn(n2));
@@ -173,9 +214,7 @@ __global__ void __launch_bounds__(kBatchThreads) batch_kernel(const BatchArgs a)
                     break;
                 }
                 case GEO_V8_NODE_SQUARED_NORM: {
-                    double sum = 0.0;
-                    if (lane == 0)
-                        for (int q = 0; q < N; ++q) sum = add(sum, mul(mul(0.5, L[q]), L[q]));
+                    const double sum = half_squared_norm(L[b0], L[b1], N);
                     o0 = lane == 0 ? sum : 0.0;
                     o1 = 0.0;
                     break;
@@ -235,15 +274,22 @@ __global__ void __launch_bounds__(kBatchThreads) batch_kernel(const BatchArgs a)
                     break;
                 case GEO_V8_NODE_GEOMETRIC_PRODUCT: {
                     // reference src/operator_kernel.c:494-539
+                    const double C0 = cot[b0], C1 = cot[b1];
+                    const double Lv0 = lvv[b0], Lv1 = lvv[b1], Rv0 = rvv[b0], Rv1 = rvv[b1];
+                    const uint64_t neg0 = a.neg[b0], neg1 = a.neg[b1];
                     double la0 = 0.0, la1 = 0.0, ra0 = 0.0, ra1 = 0.0;
-                    for (int q = 0; q < N; ++q) {
+#pragma unroll 8
+                    for (int q = 0; q < 64; ++q) {
+                        if (q >= N) break;
+                        const double cq0 = xor_first(C0, C1, q), cq1 = xor_second(C0, C1, q);  // cot[b ^ q]
+                        const double rq = blade_at(Rv0, Rv1, q), lq = blade_at(Lv0, Lv1, q);
                         if (l0) {
-                            la0 = add(la0, mul(mul(cot[b0 ^ q], gsign(a, b0, q)), rvv[q]));
-                            ra0 = add(ra0, mul(mul(cot[q ^ b0], gsign(a, q, b0)), lvv[q]));
+                            la0 = add(la0, mul(mul(cq0, ((neg0 >> q) & 1ull) ? -1.0 : 1.0), rq));
+                            ra0 = add(ra0, mul(mul(cq0, gsign(a, q, b0)), lq));
                         }
                         if (l1) {
-                            la1 = add(la1, mul(mul(cot[b1 ^ q], gsign(a, b1, q)), rvv[q]));
-                            ra1 = add(ra1, mul(mul(cot[q ^ b1], gsign(a, q, b1)), lvv[q]));
+                            la1 = add(la1, mul(mul(cq1, ((neg1 >> q) & 1ull) ? -1.0 : 1.0), rq));
+                            ra1 = add(ra1, mul(mul(cq1, gsign(a, q, b1)), lq));
                         }
                     }
                     if (ln->requires_grad) ok = accumulate2(a, lc, la0, la1, 1.0, b0, b1);
@@ -306,14 +352,8 @@ __global__ void __launch_bounds__(kBatchThreads) batch_kernel(const BatchArgs a)
                     break;
                 case GEO_V8_NODE_EUCLIDEAN_NORMALIZE: {
                     const double *ov = vals + (size_t)cursor * 64;
-                    double n2 = 0.0, dot = 0.0;
-                    if (lane == 0)
-                        for (int q = 0; q < N; ++q) {
-                            n2 = add(n2, mul(lvv[q], lvv[q]));
-                            dot = add(dot, mul(ov[q], cot[q]));
-                        }
-                    n2 = __shfl_sync(0xffffffffu, n2, 0);
-                    dot = __shfl_sync(0xffffffffu, dot, 0);
+                    const double n2 = blade_dot(lvv[b0], lvv[b1], lvv[b0], lvv[b1], N);
+                    const double dot = blade_dot(ov[b0], ov[b1], cot[b0], cot[b1], N);
                     if (!isfinite(n2) || n2 <= 0.0 || !isfinite(dot)) { ok = false; break; }
                     if (ln->requires_grad) {
                         const double inverse = __ddiv_rn(1.0, __dsqrt_rn(n2));
@@ -370,9 +410,9 @@ __global__ void reduce_partials_kernel(const double *__restrict__ partials, size
     size_t w = 0;
     for (; w + 8 <= warps; w += 8) {
         double v[8];
-#pragma unroll
+#pragma unroll 8
         for (int u = 0; u < 8; ++u) v[u] = partials[(w + u) * stride + idx];
-#pragma unroll
+#pragma unroll 8
         for (int u = 0; u < 8; ++u) acc = add(acc, v[u]);
     }
     for (; w < warps; ++w) acc = add(acc, partials[w * stride + idx]);
@@ -426,11 +466,15 @@ geo_v8_status_t run_batch(geo_v8_program_t *p, const std::vector<RowLeaf> &row_l
             }
             if (backward && n.requires_grad) b.grad_slot = slots++;
         }
+        b.invariant = leaf_kind(n.kind) ? (b.source == 0)
+                                        : (b.left >= 0 && nodes[(size_t)b.left].invariant &&
+                                           (b.right < 0 || nodes[(size_t)b.right].invariant));
+        b.reserved = 0;
     }
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GEO_V8_ALLOCATION_FAILURE;
     const int sms = device_sm_count();
-    size_t warps = (size_t)sms * (kBatchThreads / 32);
+    size_t warps = (size_t)sms * kBatchCtasPerSm * (kBatchThreads / 32);
     const size_t needed_warps = batch;
     if (warps > needed_warps) warps = needed_warps;
     if (warps < 1) warps = 1;
