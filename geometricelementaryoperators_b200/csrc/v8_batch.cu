@@ -401,22 +401,25 @@ __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(c
 }
 
 // out[r][b] = sum over warps (in warp order) of partials[w][r][b]; rows = grad_slots + 1.
+// One warp per entry: the lanes load 32 warps' partials at a time (the next
+// 32 are loaded while these are summed) and the sum runs through shuffles in
+// warp order, so the result is the sequential sum.
 __global__ void reduce_partials_kernel(const double *__restrict__ partials, size_t warps, int rows,
                                        double *__restrict__ out) {
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= rows * 64) return;
+    const int lane = threadIdx.x & 31;
+    const size_t entry = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (entry >= (size_t)rows * 64) return;  // whole warps
     const size_t stride = (size_t)rows * 64;
     double acc = 0.0;
-    size_t w = 0;
-    for (; w + 8 <= warps; w += 8) {
-        double v[8];
-#pragma unroll 8
-        for (int u = 0; u < 8; ++u) v[u] = partials[(w + u) * stride + idx];
-#pragma unroll 8
-        for (int u = 0; u < 8; ++u) acc = add(acc, v[u]);
+    double next = (size_t)lane < warps ? partials[(size_t)lane * stride + entry] : 0.0;
+    for (size_t w0 = 0; w0 < warps; w0 += 32) {
+        const double cur = next;
+        const size_t w1 = w0 + 32 + (size_t)lane;
+        next = w1 < warps ? partials[w1 * stride + entry] : 0.0;
+        const int m = warps - w0 < 32 ? (int)(warps - w0) : 32;
+        for (int j = 0; j < m; ++j) acc = add(acc, __shfl_sync(0xffffffffu, cur, j));
     }
-    for (; w < warps; ++w) acc = add(acc, partials[w * stride + idx]);
-    out[idx] = acc;
+    if (lane == 0) out[entry] = acc;
 }
 
 struct Workspace {
@@ -550,7 +553,7 @@ geo_v8_status_t run_batch(geo_v8_program_t *p, const std::vector<RowLeaf> &row_l
     std::vector<double> host_sums((size_t)rows * 64, 0.0);
     int host_flags[2] = {0, -1};
     if (e == cudaSuccess && backward) {
-        reduce_partials_kernel<<<(unsigned)((rows * 64 + 255) / 256), 256, 0, ws.stream>>>(a.partials, warps, rows,
+        reduce_partials_kernel<<<(unsigned)((rows * 64 * 32 + 255) / 256), 256, 0, ws.stream>>>(a.partials, warps, rows,
                                                                                          sums);
         e = cudaGetLastError();
         if (e == cudaSuccess)
