@@ -58,9 +58,6 @@ struct BatchArgs {
 
 __device__ __forceinline__ double mul(double a, double b) { return __dmul_rn(a, b); }
 __device__ __forceinline__ double add(double a, double b) { return __dadd_rn(a, b); }
-__device__ __forceinline__ double gsign(const BatchArgs &a, int l, int r) {
-    return ((a.neg[l] >> r) & 1ull) ? -1.0 : 1.0;
-}
 __device__ __forceinline__ int map_sign(int mode, int blade) {
     const unsigned g = __popc(blade);
     if (mode == 0) return ((g * (g - 1u) / 2u) & 1u) ? -1 : 1;  // reverse
@@ -68,6 +65,13 @@ __device__ __forceinline__ int map_sign(int mode, int blade) {
     return ((g * (g + 1u) / 2u) & 1u) ? -1 : 1;                 // Clifford conjugate
 }
 __device__ __forceinline__ bool warp_any(bool v) { return __any_sync(0xffffffffu, v); }
+
+// v * (bit `bit` of `word` set ? -1 : 1): multiplying by -1 is exact, so the
+// sign bit is flipped with an integer operation instead of an FP64 multiply.
+__device__ __forceinline__ double signed_by(double v, uint64_t word, int bit) {
+    const int flip = (int)((word >> bit) & 1ull) << 31;
+    return __hiloint2double(__double2hiint(v) ^ flip, __double2loint(v));
+}
 
 // A multivector held by a warp as (lo, hi): lane l has blades l and l + 32.
 // Blade q, on every lane:
@@ -120,11 +124,14 @@ __device__ bool accumulate2(const BatchArgs &a, double *dest, double s0, double 
     return true;
 }
 
+// NB = 2^n blades, a compile-time constant so every loop over blades has a fixed trip count.
+template <int NB>
 __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(const BatchArgs a) {
     const int lane = threadIdx.x & 31;
     const size_t warp = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const size_t warps = ((size_t)gridDim.x * blockDim.x) >> 5;
-    const int N = a.blades, C = a.count;
+    constexpr int N = NB;
+    const int C = a.count;
     double *vals = a.scratch + warp * 2 * (size_t)C * 64;
     double *cots = vals + (size_t)C * 64;
     double *part = a.partials + warp * (size_t)(a.grad_slots + 1) * 64;
@@ -176,8 +183,9 @@ __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(c
                         const double lv = blade_at(L0, L1, l);
                         const double r0 = xor_first(R0, R1, l), r1 = xor_second(R0, R1, l);
                         if (lv == 0.0) continue;
-                        if (l0) c0 = add(c0, mul(mul(lv, r0), gsign(a, l, l ^ b0)));
-                        if (l1) c1 = add(c1, mul(mul(lv, r1), gsign(a, l, l ^ b1)));
+                        const uint64_t negl = a.neg[l];
+                        if (l0) c0 = add(c0, signed_by(mul(lv, r0), negl, l ^ b0));
+                        if (l1) c1 = add(c1, signed_by(mul(lv, r1), negl, l ^ b1));
                     }
                     o0 = c0;
                     o1 = c1;
@@ -283,13 +291,14 @@ __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(c
                         if (q >= N) break;
                         const double cq0 = xor_first(C0, C1, q), cq1 = xor_second(C0, C1, q);  // cot[b ^ q]
                         const double rq = blade_at(Rv0, Rv1, q), lq = blade_at(Lv0, Lv1, q);
+                        const uint64_t negq = a.neg[q];
                         if (l0) {
-                            la0 = add(la0, mul(mul(cq0, ((neg0 >> q) & 1ull) ? -1.0 : 1.0), rq));
-                            ra0 = add(ra0, mul(mul(cq0, gsign(a, q, b0)), lq));
+                            la0 = add(la0, mul(signed_by(cq0, neg0, q), rq));
+                            ra0 = add(ra0, mul(signed_by(cq0, negq, b0), lq));
                         }
                         if (l1) {
-                            la1 = add(la1, mul(mul(cq1, ((neg1 >> q) & 1ull) ? -1.0 : 1.0), rq));
-                            ra1 = add(ra1, mul(mul(cq1, gsign(a, q, b1)), lq));
+                            la1 = add(la1, mul(signed_by(cq1, neg1, q), rq));
+                            ra1 = add(ra1, mul(signed_by(cq1, negq, b1), lq));
                         }
                     }
                     if (ln->requires_grad) ok = accumulate2(a, lc, la0, la1, 1.0, b0, b1);
@@ -547,7 +556,14 @@ geo_v8_status_t run_batch(geo_v8_program_t *p, const std::vector<RowLeaf> &row_l
         e = cudaMemcpyAsync((void *)a.leaf_values, leaf_values.data(), leaf_bytes, cudaMemcpyHostToDevice, ws.stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, 256, ws.stream);
     if (e == cudaSuccess) {
-        batch_kernel<<<(unsigned)ctas, kBatchThreads, 0, ws.stream>>>(a);
+        switch (blades) {
+            case 2: batch_kernel<2><<<(unsigned)ctas, kBatchThreads, 0, ws.stream>>>(a); break;
+            case 4: batch_kernel<4><<<(unsigned)ctas, kBatchThreads, 0, ws.stream>>>(a); break;
+            case 8: batch_kernel<8><<<(unsigned)ctas, kBatchThreads, 0, ws.stream>>>(a); break;
+            case 16: batch_kernel<16><<<(unsigned)ctas, kBatchThreads, 0, ws.stream>>>(a); break;
+            case 32: batch_kernel<32><<<(unsigned)ctas, kBatchThreads, 0, ws.stream>>>(a); break;
+            default: batch_kernel<64><<<(unsigned)ctas, kBatchThreads, 0, ws.stream>>>(a); break;
+        }
         e = cudaGetLastError();
     }
     std::vector<double> host_sums((size_t)rows * 64, 0.0);
