@@ -75,8 +75,14 @@ geo_batch_gp_cuda_status_t vjp(const geo_batch_gp_cuda_plan_t *plan, const doubl
     if (sp == nullptr) return GEO_BATCH_GP_CUDA_INVALID_ARGUMENT;
     double *records = plan_records(plan);
     int ctas = 0;
-    cudaError_t e = geo::launch_cycle(*sp, geo::kVjp, device_inputs, device_output_cotangents, nullptr, nullptr,
-                                      batch_size, records, &ctas, stream);
+    // n = 5, 6 with 16-byte aligned operands: the representation kernel on the
+    // FP64 tensor cores; otherwise the Cayley kernel.
+    const geo::RepDevice *rep = geo::cached_rep_device(plan->dimension, plan->signature, parameter_on_left != 0);
+    cudaError_t e = (rep != nullptr && geo::rep_vjp_supported(*rep, device_inputs, device_output_cotangents))
+                        ? geo::launch_rep_vjp(*rep, device_inputs, device_output_cotangents, batch_size, records,
+                                              &ctas, stream)
+                        : geo::launch_cycle(*sp, geo::kVjp, device_inputs, device_output_cotangents, nullptr, nullptr,
+                                            batch_size, records, &ctas, stream);
     if (e != cudaSuccess) return launch_status(e);
     geo::OptimizerArgs opt{};
     opt.kind = geo::kOptNone;

@@ -157,9 +157,12 @@ geo_batch_gp_status_t vjp_impl(const geo_batch_gp_plan_t *plan, const double *in
     int ctas = 0;
     uint32_t bits = 0;
     double gradient[64];
+    const geo::RepDevice *rep = geo::cached_rep_device(plan->dimension, plan->signature, on_left != 0);
+    const bool use_rep = rep != nullptr && geo::rep_vjp_supported(*rep, ws.a, ws.b);
     if (cudaMemsetAsync(ws.status, 0, sizeof(uint32_t), ws.stream) != cudaSuccess ||
-        geo::launch_cycle(*sp, geo::kVjp, ws.a, ws.b, nullptr, nullptr, batch_size, ws.records, &ctas, ws.stream) !=
-            cudaSuccess ||
+        (use_rep ? geo::launch_rep_vjp(*rep, ws.a, ws.b, batch_size, ws.records, &ctas, ws.stream)
+                 : geo::launch_cycle(*sp, geo::kVjp, ws.a, ws.b, nullptr, nullptr, batch_size, ws.records, &ctas,
+                                     ws.stream)) != cudaSuccess ||
         geo::launch_finalize(ws.records, ctas, opt, ws.small + 64, nullptr, nullptr, nullptr, nullptr, ws.status,
                              ws.stream) != cudaSuccess ||
         geo::copy_any(&bits, ws.status, sizeof(bits), ws.stream) != cudaSuccess ||

@@ -172,5 +172,13 @@ bool rep_supported(const RepDevice &rep);
 cudaError_t launch_rep_cycle(const RepDevice &rep, const double *inputs, const double *targets,
                              const double *parameter, size_t batch, double *records, int *ctas_used,
                              cudaStream_t stream);
+// Parameter VJP of output cotangents through the representation (record
+// contract of launch_cycle(kVjp)); needs 16-byte aligned inputs and cotangents.
+bool rep_vjp_supported(const RepDevice &rep, const double *inputs, const double *cotangents);
+cudaError_t launch_rep_vjp(const RepDevice &rep, const double *inputs, const double *cotangents, size_t batch,
+                           double *records, int *ctas_used, cudaStream_t stream);
+// Representation tables for (dimension, signature, side), built once and cached;
+// null when the algebra has no warp-specialised representation kernel (n < 5).
+const RepDevice *cached_rep_device(uint8_t dimension, const int8_t *signature, bool parameter_on_left);
 
 }  // namespace geo

@@ -475,7 +475,10 @@ __device__ __forceinline__ void walsh(double (&w)[S]) {
             }
 }
 
-template <int D, int S>
+// VJP = false: training pass (x, targets t, parameter W). VJP = true: parameter
+// VJP of given output cotangents c (in place of t, no W): the producers write
+// C' = P c instead of -T', and GEMM 1 is skipped (R' := C').
+template <int D, int S, bool VJP>
 __global__ void __launch_bounds__(kWsThreads, 2)
 rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ T,
               const double *__restrict__ W, size_t batch, double *__restrict__ records) {
@@ -497,7 +500,7 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
         s_gave_up = 0u;
     }
     // W' = rho(W) (right) or rho(W)^T (left), as in rep_cycle_kernel.
-    for (int idx = tid; idx < D * D; idx += kWsThreads) {
+    for (int idx = tid; !VJP && idx < D * D; idx += kWsThreads) {
         const int k = idx / D, j = idx - k * D;
         const int col = rep.side ? k : j;
         double acc = 0.0;
@@ -590,7 +593,7 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
 #pragma unroll
                 for (int f = 0; f < S; ++f) {
                     xs[G::SLOTS * i * N + woff[f]] = flip_sign(vx[i][f], out_sign[f]);
-                    ts[G::SLOTS * i * N + woff[f]] = flip_sign(vt[i][f], out_sign[f] ^ 0x80000000u);  // -T
+                    ts[G::SLOTS * i * N + woff[f]] = flip_sign(vt[i][f], out_sign[f] ^ (VJP ? 0u : 0x80000000u));  // -T' or C'
                 }
             }
             named_arrive(kBarFull + st, kWsThreads);
@@ -605,7 +608,8 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
         double wa[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            if (D == 16) wa[i] = Wp[(t4 + 4 * (i / 2)) * D + g + 8 * (i % 2)];
+            if (VJP) wa[i] = 0.0;
+            else if (D == 16) wa[i] = Wp[(t4 + 4 * (i / 2)) * D + g + 8 * (i % 2)];
             else wa[i] = i < KT ? Wp[(4 * i + t4) * D + g] : 0.0;
         }
         for (int k = 0; k < K; ++k) {
@@ -632,7 +636,7 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
                             c[q][h] = ts[ws_index<D>(n0[q] + 2 * t4 + h, g)];
                             c[q][2 + h] = ts[ws_index<D>(n0[q] + 2 * t4 + h, g + 8)];
                         }
-                        mma_16x8x16(c[q], wa, b);
+                        if constexpr (!VJP) mma_16x8x16(c[q], wa, b);
                     }
                     // Epilogue in registers; GEMM 2 over both row groups as one m16n8k16 per
                     // 8-column tile of G', k slot t + 4 j <-> row n0[j / 2] + 2 t + j % 2.
@@ -659,7 +663,7 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
 #pragma unroll
                         for (int h = 0; h < 2; ++h) c[q][h] = ts[ws_index<D>(n0[q] + 2 * t4 + h, g)];
 #pragma unroll
-                    for (int kk = 0; kk < KT; ++kk)
+                    for (int kk = 0; !VJP && kk < KT; ++kk)
 #pragma unroll
                         for (int q = 0; q < 2; ++q) mma_8x8x4(c[q], wa[kk], xs[ws_index<D>(n0[q] + g, 4 * kk + t4)]);
 #pragma unroll
@@ -727,12 +731,12 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
     }
 }
 
-template <int D, int S>
+template <int D, int S, bool VJP>
 cudaError_t launch_rep_ws(const RepDevice &rep, const double *X, const double *T, const double *W, size_t batch,
                           double *records, int *ctas_used, cudaStream_t stream) {
     using G = WsGeo<D, S>;
     if (rep.raw_stride != G::N || rep.D != D || rep.S != S) return cudaErrorInvalidValue;
-    auto kernel = rep_ws_kernel<D, S>;
+    auto kernel = rep_ws_kernel<D, S, VJP>;
     const size_t smem = (size_t)(D * D + kWsStages * G::STAGE) * sizeof(double) + kWsStages * sizeof(uint64_t);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -752,23 +756,33 @@ cudaError_t launch_rep_ws(const RepDevice &rep, const double *X, const double *T
 
 }  // namespace
 
-bool rep_supported(const RepDevice &rep) {
-    return (rep.D == 16 && rep.S == 4) || (rep.D == 8 && rep.S == 8) || (rep.D == 8 && rep.S == 4) ||
-           (rep.D == 16 && rep.S == 2);
-}
-
 cudaError_t launch_rep_cycle(const RepDevice &rep, const double *X, const double *T, const double *W, size_t batch,
                              double *records, int *ctas_used, cudaStream_t stream) {
     const bool al = (((uintptr_t)X | (uintptr_t)T) & 15u) == 0u;
 #define GEO_REP_CASE(DD, SS)                                                                             \
     if (rep.D == DD && rep.S == SS)                                                                      \
-        return (al && rep.ws_ready) ? launch_rep_ws<DD, SS>(rep, X, T, W, batch, records, ctas_used, stream) \
+        return (al && rep.ws_ready) ? launch_rep_ws<DD, SS, false>(rep, X, T, W, batch, records, ctas_used, stream) \
                   : launch_rep_impl<DD, SS, false>(rep, X, T, W, batch, records, ctas_used, stream);
     GEO_REP_CASE(16, 4)
     GEO_REP_CASE(8, 8)
     GEO_REP_CASE(8, 4)
     GEO_REP_CASE(16, 2)
 #undef GEO_REP_CASE
+    return cudaErrorInvalidValue;
+}
+
+
+bool rep_vjp_supported(const RepDevice &rep, const double *X, const double *C) {
+    return rep.ws_ready && rep_supported(rep) && (((uintptr_t)X | (uintptr_t)C) & 15u) == 0u;
+}
+
+cudaError_t launch_rep_vjp(const RepDevice &rep, const double *X, const double *C, size_t batch, double *records,
+                           int *ctas_used, cudaStream_t stream) {
+    if (!rep_vjp_supported(rep, X, C)) return cudaErrorInvalidValue;
+    if (rep.D == 16 && rep.S == 4) return launch_rep_ws<16, 4, true>(rep, X, C, nullptr, batch, records, ctas_used, stream);
+    if (rep.D == 8 && rep.S == 8) return launch_rep_ws<8, 8, true>(rep, X, C, nullptr, batch, records, ctas_used, stream);
+    if (rep.D == 8 && rep.S == 4) return launch_rep_ws<8, 4, true>(rep, X, C, nullptr, batch, records, ctas_used, stream);
+    if (rep.D == 16 && rep.S == 2) return launch_rep_ws<16, 2, true>(rep, X, C, nullptr, batch, records, ctas_used, stream);
     return cudaErrorInvalidValue;
 }
 

@@ -3,6 +3,7 @@
 #include "representation.h"
 
 #include <cstring>
+#include <mutex>
 #include <utility>
 #include <vector>
 
@@ -384,6 +385,38 @@ bool make_rep_device(RepDevice *out, const RepPlan &p) {
     // D = 16, S >= 2 and D = 8, S >= 4; without tables the synchronous kernel runs).
     if ((D == 16 && S >= 2) || (D == 8 && S >= 4)) out->ws_ready = make_ws_tables(out, p, members) ? 1 : 0;
     return true;
+}
+
+bool rep_supported(const RepDevice &rep) {
+    return (rep.D == 16 && rep.S == 4) || (rep.D == 8 && rep.S == 8) || (rep.D == 8 && rep.S == 4) ||
+           (rep.D == 16 && rep.S == 2);
+}
+
+namespace {
+// Index: dimension (5, 6) x signature bit pattern (bit a set = axis a is -1) x side.
+struct RepSlot {
+    bool tried = false;
+    bool usable = false;
+    RepDevice rep;
+};
+RepSlot g_rep_slots[2][64][2];
+std::mutex g_rep_mutex;
+}  // namespace
+
+const RepDevice *cached_rep_device(uint8_t dimension, const int8_t *signature, bool parameter_on_left) {
+    if (dimension < 5 || dimension > kMaxDim || !signature_valid(signature, dimension)) return nullptr;
+    unsigned mask = 0;
+    for (unsigned a = 0; a < dimension; ++a)
+        if (signature[a] < 0) mask |= 1u << a;
+    RepSlot &slot = g_rep_slots[dimension - 5][mask][parameter_on_left ? 1 : 0];
+    std::lock_guard<std::mutex> lock(g_rep_mutex);
+    if (!slot.tried) {
+        slot.tried = true;
+        RepPlan rp;
+        slot.usable = make_rep_plan(&rp, dimension, signature, parameter_on_left ? 1 : 0) &&
+                      make_rep_device(&slot.rep, rp) && rep_supported(slot.rep) && slot.rep.ws_ready;
+    }
+    return slot.usable ? &slot.rep : nullptr;
 }
 
 }  // namespace geo
