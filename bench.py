@@ -37,6 +37,7 @@ METRIC = "multivector products/s and training samples/s at Cl(6,0), % of HBM/FP6
 UNIT = "training samples/s"
 BYTES_PER_SAMPLE = 2 * 64 * 8     # read x and t once per step (float64, 64 blades)
 FLOPS_PER_SAMPLE = 4 * 64 * 64    # forward 2*4^n + parameter VJP 2*4^n
+FORWARD_BYTES_PER_SAMPLE = 2 * 64 * 8  # forward: read x, write y
 
 
 def parse():
@@ -48,7 +49,7 @@ def parse():
     p.add_argument("--batch-log2", type=int, default=22, help="per-GPU batch = 2^k (22 is the headline shape)")
     p.add_argument("--negative", type=int, default=0, help="q of Cl(6-q, q); 0 = Cl(6,0)")
     p.add_argument("--no-extras", action="store_true", help="skip e2e, Cl(3,3) and cpu_baseline legs")
-    p.add_argument("--leg", choices=["train", "pairwise-f32", "v8-graph"], default="train",
+    p.add_argument("--leg", choices=["train", "pairwise-f32", "v8-graph", "forward"], default="train",
                    help="pairwise-f32: run only the float32 pairwise sweep (for profiling)")
     p.add_argument("--pairwise-log2", type=int, default=26, help="batch 2^k of the float32 pairwise sweep")
     p.add_argument("--algorithm", choices=["auto", "cayley", "representation"], default="auto",
@@ -440,6 +441,63 @@ def pairwise_f32_leg(lib, args, world) -> dict:
             "hbm_frac": gbs / hbm_peak, "flops_per_product": 2 * 32 * 64}
 
 
+def forward_leg(lib, X, q, world) -> dict:
+    """Fixed-parameter forward y = x*W, Cl(6-q,q), float64, on the batch already
+    resident for the training step (2 GiB of x read, 2 GiB of y written per
+    launch, far above L2): geo_b200_forward_f64 on the representation kernel,
+    and the device ABI's planned forward (Cayley kernel) beside it."""
+    import torch
+
+    from geometricelementaryoperators_b200 import abi
+
+    batch = X.shape[0]
+    sig = [1] * (6 - q) + [-1] * q
+    w = torch.randn(64, dtype=torch.float64, device="cuda", generator=torch.Generator(device="cuda").manual_seed(9))
+    Y = torch.empty_like(X)
+    stream = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    xp, wp, yp = (ctypes.c_void_p(t.data_ptr()) for t in (X, w, Y))
+    plan = abi.BatchGpPlan()
+    assert lib.geo_batch_gp_plan_init(ctypes.byref(plan), 6, abi.sig_array(sig)) == 0
+    cplan = abi.CudaPlan()
+    assert lib.geo_batch_gp_cuda_plan_upload(ctypes.byref(cplan), ctypes.byref(plan)) == 0
+    calls = {
+        "representation": lambda: lib.geo_b200_forward_f64(6, abi.sig_array(sig), 0, 2, xp, wp, yp, batch, sp),
+        "cayley_device_abi": lambda: lib.geo_batch_gp_cuda_planned_forward_f64(ctypes.byref(cplan), xp, batch, wp,
+                                                                              0, yp, sp),
+    }
+    out = {}
+    hbm_peak, _ = peaks()
+    for name, call in calls.items():
+        for _ in range(3):
+            assert call() == 0
+        torch.cuda.synchronize()
+        barrier(world)
+        reps = 10
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(reps):
+            assert call() == 0
+        e.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(s.elapsed_time(e) / reps, world)
+        gbs = batch * FORWARD_BYTES_PER_SAMPLE / (ms / 1e3) / 1e9
+        out[name] = {"value": batch * world / (ms / 1e3), "unit": "products/s", "ms_per_launch": ms,
+                     "achieved_gbs": gbs, "hbm_frac": gbs / hbm_peak}
+    lib.geo_batch_gp_cuda_plan_destroy(ctypes.byref(cplan))
+    del Y
+    torch.cuda.empty_cache()
+    best = out["representation"]
+    return {"workload": f"Cl({6 - q},{q}) fixed-parameter forward y = x*W, float64, batch 2^{int(math.log2(batch))} "
+                        "per GPU (x resident, 2 GiB read + 2 GiB written per launch; no flush needed)",
+            "value": best["value"], "unit": "products/s", "bytes_per_product": FORWARD_BYTES_PER_SAMPLE,
+            "roofline": {"bound": "hbm", "achieved": best["achieved_gbs"], "peak": hbm_peak, "unit": "GB/s",
+                         "frac": best["hbm_frac"],
+                         "kernel": "rep_fwd_kernel<" + ("16, 4" if q in (0, 1, 5, 6) else "8, 8") +
+                                   "> (representation forward, FP64 tensor cores), CUDA events on the launch stream"},
+            "kernels": out}
+
+
 # --------------------------------------------------------------------------- main arm
 def run_b200(args, world, rank, local):
     import numpy as np
@@ -543,6 +601,8 @@ def run_b200(args, world, rank, local):
         # (compact, 32 floats), dense right operand; HBM-bound sweep.
         extras["pairwise_f32"] = pairwise_f32_leg(lib, args, world)
         extras["v8_graph"] = v8_graph_leg(args, world)
+        # Fixed-parameter forward (multivector products/s) on the same resident batch.
+        extras["forward"] = forward_leg(lib, X, q, world)
         # Same step on Cl(3,3) (the second signature of the headline config).
         X2, T2, w2 = X, T, w0
         tr33 = Trainer(lib, [1, 1, 1, -1, -1, -1], w2)
@@ -617,6 +677,8 @@ def run_b200(args, world, rank, local):
             line["pairwise_f32"] = extras["pairwise_f32"]
         if "v8_graph" in extras:
             line["v8_graph"] = extras["v8_graph"]
+        if "forward" in extras:
+            line["forward"] = extras["forward"]
         if world == 1 and not args.no_extras:
             line["cpu_baseline"] = cpu_baseline_leg(q)
             line["v8_graph"]["cpu_baseline"] = v8_graph_reference_leg()
@@ -642,6 +704,17 @@ def main():
             if rank == 0:
                 if world == 1:
                     res["cpu_baseline"] = v8_graph_reference_leg()
+                print(json.dumps(res), flush=True)
+            return
+        if args.leg == "forward":
+            import torch
+
+            from geometricelementaryoperators_b200 import abi
+
+            gen = torch.Generator(device="cuda").manual_seed(5)
+            X = torch.rand((1 << args.batch_log2, 64), dtype=torch.float64, device="cuda", generator=gen)
+            res = forward_leg(abi.lib(), X.mul_(2).sub_(1), args.negative, world)
+            if rank == 0:
                 print(json.dumps(res), flush=True)
             return
         if args.leg == "pairwise-f32":

@@ -138,6 +138,7 @@ SIGNATURES: dict[str, tuple] = {
     "geo_b200_trainer_device_parameter": (_P, [_P]),
     "geo_b200_trainer_set_algorithm": (_I, [_P, _I]),
     "geo_b200_trainer_algorithm": (_I, [_P]),
+    "geo_b200_forward_f64": (_I, [_U8, _I8P, _I, _I, _P, _P, _P, _SZ, _P]),
     "geo_b200_comm_unique_id": (_I, [_P]),
     "geo_b200_comm_create": (_I, [ctypes.POINTER(_P), _I, _I, _P, _I]),
     "geo_b200_comm_destroy": (None, [_P]),

@@ -177,6 +177,11 @@ cudaError_t launch_rep_cycle(const RepDevice &rep, const double *inputs, const d
 bool rep_vjp_supported(const RepDevice &rep, const double *inputs, const double *cotangents);
 cudaError_t launch_rep_vjp(const RepDevice &rep, const double *inputs, const double *cotangents, size_t batch,
                            double *records, int *ctas_used, cudaStream_t stream);
+// Forward y = x W (or W x) through the representation; needs 16-byte aligned
+// inputs and outputs (outputs may equal inputs, but must not overlap them otherwise).
+bool rep_forward_supported(const RepDevice &rep, const double *inputs, const double *outputs);
+cudaError_t launch_rep_forward(const RepDevice &rep, const double *inputs, const double *parameter, double *outputs,
+                               size_t batch, cudaStream_t stream);
 // Representation tables for (dimension, signature, side), built once and cached;
 // null when the algebra has no warp-specialised representation kernel (n < 5).
 const RepDevice *cached_rep_device(uint8_t dimension, const int8_t *signature, bool parameter_on_left);

@@ -754,7 +754,275 @@ cudaError_t launch_rep_ws(const RepDevice &rep, const double *X, const double *T
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Forward through the representation (16-byte aligned x and y).
+//
+// Per sample: X' = P x, Y' = X' W', y = P^-1 Y'. P is block diagonal over the
+// blade groups, and a group's S x S block is O H I (O, I diagonal signs, H the
+// Walsh-Hadamard matrix, H H = S 1), so its inverse is I H O / S: the scatter
+// runs the gather's butterfly backwards (read the kept entries, flip by the
+// output signs, Walsh transform, flip by the input signs, scale by 1/S, which
+// is exact).
+//
+// Warps 0-3 (producers): thread 0 keeps kFwdAhead bulk loads of raw x tiles in
+// flight (completion on one mbarrier per stage). For tile k all producers
+// gather X' in place and arrive on full[stage]; then, once the consumers have
+// arrived on done[] for tile k - kFwdLag, they scatter its Y' back to raw rows
+// in place, and thread 0 stores the tile's rows with one bulk copy. A stage is
+// reloaded only after its store has finished reading it (bulk wait_group.read).
+// Warps 4-7 (consumers): GEMM 1 transposed with W'^T fragments resident, as in
+// rep_ws_kernel, from zero accumulators; Y' is written over the X' rows the
+// warp has just read.
+// Every wait is bounded; a wait that gives up makes the CTA write NaN in place
+// of its remaining outputs, and the kernel still ends.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_store(void *dst, const void *src, unsigned bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(dst), "r"(smem_u32(src)),
+                 "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int D, int S>
+__global__ void __launch_bounds__(kWsThreads, 2)
+rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ W, size_t batch,
+               double *Y) {
+    using G = WsGeo<D, S>;
+    constexpr int N = G::N, TS = G::TS, TILE = G::TILE;
+    constexpr int kConsumers = kWsThreads - kWsProducers;
+    constexpr int kBarScatter = 1;  // named barrier of the producer warps
+    extern __shared__ __align__(16) double smem[];
+    double *Wp = smem;                      // D * D
+    double *stages = Wp + D * D;            // kFwdStages x one x tile
+    uint64_t *loaded = reinterpret_cast<uint64_t *>(stages + kFwdStages * TILE);
+    uint64_t *full = loaded + kFwdStages;   // producers -> consumers: X' ready
+    uint64_t *done = full + kFwdStages;     // consumers -> producers: Y' ready
+    __shared__ unsigned s_gave_up;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t tiles = (batch + TS - 1) / TS;
+    const int K = (size_t)blockIdx.x < tiles ? (int)((tiles - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+
+    if (tid == 0) {
+        for (int s = 0; s < kFwdStages; ++s) {
+            mbar_init(&loaded[s], 1);
+            mbar_init(&full[s], kWsProducers);
+            mbar_init(&done[s], kConsumers);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        s_gave_up = 0u;
+    }
+    // W' = rho(W) (right) or rho(W)^T (left), as in rep_cycle_kernel.
+    for (int idx = tid; idx < D * D; idx += kWsThreads) {
+        const int k = idx / D, j = idx - k * D;
+        const int col = rep.side ? k : j;
+        double acc = 0.0;
+        for (int A = 0; A < N; ++A) {
+            if (rep.xm[A] != (k ^ j)) continue;
+            const double w = W[A];
+            const bool neg = (rep.sg[A] < 0) != ((__popc(rep.zm[A] & col) & 1) != 0);
+            acc += neg ? -w : w;
+        }
+        Wp[idx] = acc;
+    }
+    __syncthreads();
+
+    if (warp < kWsProducers / 32) {
+        // ------------------------------------------------------------ producers
+        const int m = tid % D, slot = tid / D;
+        const int L = D == 8 ? (slot & 1) * 8 + m : m;
+        int roff[S], woff[S];
+        unsigned in_sign[S], out_sign[S];
+#pragma unroll
+        for (int t = 0; t < S; ++t) {
+            roff[t] = slot * N + rep.ws_blade[L][t];
+            in_sign[t] = ((rep.ws_in_neg[L] >> t) & 1u) << 31;
+            const int r = rep.ws_out_row[L][t];
+            woff[t] = ws_index<D>(slot * S + r, rep.grp_col[m][r]);
+            out_sign[t] = ((rep.ws_out_neg[L] >> t) & 1u) << 31;
+        }
+        const double inv_s = 1.0 / (double)S;  // exact: S is a power of two
+        auto tile_rows = [&](int k, size_t *first) {
+            *first = (blockIdx.x + (size_t)k * gridDim.x) * TS;
+            return batch - *first < (size_t)TS ? (int)(batch - *first) : TS;
+        };
+        auto issue = [&](int k) {
+            size_t first;
+            const unsigned bytes = (unsigned)tile_rows(k, &first) * N * (unsigned)sizeof(double);
+            uint64_t *bar = &loaded[k % kFwdStages];
+            mbar_expect_tx(bar, bytes);
+            bulk_load(stages + (k % kFwdStages) * TILE, X + first * N, bytes, bar);
+        };
+        if (tid == 0)
+            for (int k = 0; k < K && k < kFwdAhead; ++k) issue(k);
+        for (int k = 0; k < K + kFwdLag; ++k) {
+            if (k < K) {
+                const int ahead = k + kFwdAhead;
+                if (tid == 0 && ahead < K) {
+                    // The stage of `ahead` last held tile ahead - kFwdStages, whose store was
+                    // issued kFwdStorePending stores ago at the latest.
+                    if (ahead >= kFwdStages) bulk_wait_read<kFwdStorePending>();
+                    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                    issue(ahead);
+                }
+                const int st = k % kFwdStages;
+                if (!mbar_wait(&loaded[st], (unsigned)((k / kFwdStages) & 1))) atomicOr(&s_gave_up, 1u);
+                size_t first;
+                const int valid = tile_rows(k, &first);
+                double *xs = stages + st * TILE;
+                double v[G::PER][S];
+#pragma unroll
+                for (int i = 0; i < G::PER; ++i) {
+                    const bool ok = slot + G::SLOTS * i < valid;
+#pragma unroll
+                    for (int t = 0; t < S; ++t) v[i][t] = ok ? xs[G::SLOTS * i * N + roff[t]] : 0.0;
+                }
+                named_sync(kBarScatter, kWsProducers);  // every raw read is done before the in-place writes
+#pragma unroll
+                for (int i = 0; i < G::PER; ++i) {
+#pragma unroll
+                    for (int t = 0; t < S; ++t) v[i][t] = flip_sign(v[i][t], in_sign[t]);
+                    walsh<S>(v[i]);
+#pragma unroll
+                    for (int f = 0; f < S; ++f) xs[G::SLOTS * i * N + woff[f]] = flip_sign(v[i][f], out_sign[f]);
+                }
+                mbar_arrive(&full[st]);
+            }
+            const int j = k - kFwdLag;
+            if (j >= 0) {
+                const int st = j % kFwdStages;
+                if (!mbar_wait(&done[st], (unsigned)((j / kFwdStages) & 1))) atomicOr(&s_gave_up, 1u);
+                double *xs = stages + st * TILE;
+                double v[G::PER][S];
+#pragma unroll
+                for (int i = 0; i < G::PER; ++i)
+#pragma unroll
+                    for (int f = 0; f < S; ++f) v[i][f] = flip_sign(xs[G::SLOTS * i * N + woff[f]], out_sign[f]);
+                named_sync(kBarScatter, kWsProducers);  // every Y' read is done before the in-place writes
+                const bool poison = *(volatile unsigned *)&s_gave_up != 0u;
+#pragma unroll
+                for (int i = 0; i < G::PER; ++i) {
+                    walsh<S>(v[i]);
+#pragma unroll
+                    for (int t = 0; t < S; ++t)
+                        xs[G::SLOTS * i * N + roff[t]] =
+                            poison ? __longlong_as_double(0x7ff8000000000000ll) : flip_sign(v[i][t], in_sign[t]) * inv_s;
+                }
+                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic writes -> bulk store
+                named_sync(kBarScatter, kWsProducers);
+                if (tid == 0) {
+                    size_t first;
+                    const int valid = tile_rows(j, &first);
+                    bulk_store(Y + first * N, xs, (unsigned)valid * N * (unsigned)sizeof(double));
+                }
+            }
+        }
+        if (tid == 0) {
+            asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+            // After a wait that gave up, bounded waits for loads that may still be in flight.
+            if (*(volatile unsigned *)&s_gave_up != 0u)
+                for (int k = K > kFwdStages ? K - kFwdStages : 0; k < K; ++k)
+                    (void)mbar_wait(&loaded[k % kFwdStages], (unsigned)((k / kFwdStages) & 1));
+        }
+    } else {
+        // ------------------------------------------------------------ consumers
+        const int cw = warp - kWsProducers / 32;
+        const int g = lane >> 2, t4 = lane & 3;
+        constexpr int KT = D / 4;
+        double wa[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (D == 16) wa[i] = Wp[(t4 + 4 * (i / 2)) * D + g + 8 * (i % 2)];
+            else wa[i] = i < KT ? Wp[(4 * i + t4) * D + g] : 0.0;
+        }
+        for (int k = 0; k < K; ++k) {
+            const int st = k % kFwdStages;
+            if (!mbar_wait(&full[st], (unsigned)((k / kFwdStages) & 1))) atomicOr(&s_gave_up, 1u);
+            double *xs = stages + st * TILE;
+#pragma unroll
+            for (int j = 0; j < G::GPW; j += 2) {
+                int n0[2];
+                n0[0] = (cw * G::GPW + j) * 8;
+                n0[1] = n0[0] + 8;
+                if constexpr (D == 16) {
+                    double c[2][4];
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        double b[4];
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk) b[kk] = xs[ws_index<D>(n0[q] + g, 4 * kk + t4)];
+                        c[q][0] = c[q][1] = c[q][2] = c[q][3] = 0.0;
+                        mma_16x8x16(c[q], wa, b);
+                    }
+                    __syncwarp();  // the warp's X' reads of these rows are done before Y' overwrites them
+#pragma unroll
+                    for (int q = 0; q < 2; ++q)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            xs[ws_index<D>(n0[q] + 2 * t4 + h, g)] = c[q][h];
+                            xs[ws_index<D>(n0[q] + 2 * t4 + h, g + 8)] = c[q][2 + h];
+                        }
+                } else {
+                    double c[2][2] = {{0.0, 0.0}, {0.0, 0.0}};
+#pragma unroll
+                    for (int kk = 0; kk < KT; ++kk)
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) mma_8x8x4(c[q], wa[kk], xs[ws_index<D>(n0[q] + g, 4 * kk + t4)]);
+                    __syncwarp();
+#pragma unroll
+                    for (int q = 0; q < 2; ++q)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) xs[ws_index<D>(n0[q] + 2 * t4 + h, g)] = c[q][h];
+                }
+            }
+            mbar_arrive(&done[st]);
+        }
+    }
+}
+
+template <int D, int S>
+cudaError_t launch_rep_fwd(const RepDevice &rep, const double *X, const double *W, double *Y, size_t batch,
+                           cudaStream_t stream) {
+    using G = WsGeo<D, S>;
+    if (rep.raw_stride != G::N || rep.D != D || rep.S != S) return cudaErrorInvalidValue;
+    auto kernel = rep_fwd_kernel<D, S>;
+    const size_t smem =
+        (size_t)(D * D + kFwdStages * G::TILE) * sizeof(double) + 3 * kFwdStages * sizeof(uint64_t);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kWsThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    const size_t tiles = (batch + G::TS - 1) / G::TS;
+    size_t grid = (size_t)device_sm_count() * (size_t)per_sm;
+    if (grid > tiles) grid = tiles;
+    if (grid < 1) grid = 1;
+    kernel<<<(unsigned)grid, kWsThreads, smem, stream>>>(rep, X, W, batch, Y);
+    return cudaGetLastError();
+}
+
 }  // namespace
+
+bool rep_forward_supported(const RepDevice &rep, const double *X, const double *Y) {
+    return rep.ws_ready && rep_supported(rep) && (((uintptr_t)X | (uintptr_t)Y) & 15u) == 0u;
+}
+
+cudaError_t launch_rep_forward(const RepDevice &rep, const double *X, const double *W, double *Y, size_t batch,
+                               cudaStream_t stream) {
+    if (!rep_forward_supported(rep, X, Y)) return cudaErrorInvalidValue;
+    if (rep.D == 16 && rep.S == 4) return launch_rep_fwd<16, 4>(rep, X, W, Y, batch, stream);
+    if (rep.D == 8 && rep.S == 8) return launch_rep_fwd<8, 8>(rep, X, W, Y, batch, stream);
+    if (rep.D == 8 && rep.S == 4) return launch_rep_fwd<8, 4>(rep, X, W, Y, batch, stream);
+    if (rep.D == 16 && rep.S == 2) return launch_rep_fwd<16, 2>(rep, X, W, Y, batch, stream);
+    return cudaErrorInvalidValue;
+}
 
 cudaError_t launch_rep_cycle(const RepDevice &rep, const double *X, const double *T, const double *W, size_t batch,
                              double *records, int *ctas_used, cudaStream_t stream) {

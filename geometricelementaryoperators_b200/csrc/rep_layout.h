@@ -17,6 +17,18 @@ constexpr int kWsThreads = 256;    // 8 warps per CTA
 constexpr int kWsProducers = 128;  // warps 0-3: bulk loads and gathers
 constexpr int kWsStages = 6;       // shared-memory stages per CTA
 
+// Forward kernel (rep_fwd_kernel): a stage holds one x tile (8 KB), which is
+// gathered in place, overwritten by Y', scattered back to raw y rows and
+// stored from the same stage.
+constexpr int kFwdStages = 12;  // shared-memory stages per CTA
+constexpr int kFwdAhead = 7;    // tiles whose bulk loads are in flight
+constexpr int kFwdLag = 2;      // the scatter of tile k - kFwdLag follows the gather of tile k
+// Bulk stores that may still be reading shared memory when a stage is
+// reloaded: the load of tile k + kFwdAhead reuses the stage of tile
+// k + kFwdAhead - kFwdStages, whose store was issued this many stores ago.
+constexpr int kFwdStorePending = kFwdStages - 1 - kFwdLag - kFwdAhead;
+static_assert(kFwdStorePending >= 0, "a stage is reloaded only after its store was issued");
+
 template <int D, int S>
 struct WsGeo {
     static constexpr int N = D * S;                // blades = doubles per sample

@@ -145,6 +145,28 @@ geo_b200_algorithm_t geo_b200_trainer_algorithm(const geo_b200_trainer_t *traine
 /* Device pointer to the resident parameter (2^n doubles). */
 const double *geo_b200_trainer_device_parameter(const geo_b200_trainer_t *trainer);
 
+/* ---- 1b. fixed-parameter forward on a chosen kernel family ------------ */
+
+/* outputs[s] = inputs[s] * parameter (parameter_on_left = 0) or
+ * parameter * inputs[s]: the product of geo_batch_gp_cuda_planned_forward_f64
+ * (reference src/batch_gp_cuda.cu:252-286, src/batch_gp.c:107-161) without a
+ * plan object. All arrays are device memory; asynchronous on `stream`;
+ * reports argument and launch errors only, like the device ABI.
+ *  CAYLEY: the kernel behind the device ABI's forward, bit-identical to it.
+ *  REPRESENTATION (n = 5, 6; inputs and outputs 16-byte aligned): X' = P x,
+ *    Y' = X' W' on FP64 tensor cores, y = P^-1 Y'. Equal to the Cayley product
+ *    up to rounding (within 1e-12 relative); INVALID_ARGUMENT where it is not
+ *    available.
+ *  AUTO: REPRESENTATION where available, else CAYLEY.
+ * device_parameter may be geo_b200_trainer_device_parameter(). Outputs may be
+ * the inputs (in place) but must not overlap them otherwise. A non-finite
+ * input coefficient makes every output coefficient of its sample non-finite
+ * on both families, as in the reference (which of Inf and NaN may differ). */
+geo_b200_status_t geo_b200_forward_f64(uint8_t dimension, const int8_t *signature, int parameter_on_left,
+                                       geo_b200_algorithm_t algorithm, const double *device_inputs,
+                                       const double *device_parameter, double *device_outputs, size_t batch_size,
+                                       cudaStream_t stream);
+
 /* ---- 2. data parallelism ---------------------------------------------- */
 
 #define GEO_B200_COMM_ID_BYTES 128

@@ -78,7 +78,86 @@ static const char *check_ws_layout(const RepDevice &dev) {
                     }
             }
         }
+    // rep_fwd_kernel: the consumers' Y' writes (the epilogue positions above)
+    // cover every transformed entry of the tile exactly once.
+    std::vector<int> ywrites(G::TILE, 0);
+    for (int cw = 0; cw < 4; ++cw)
+        for (int j = 0; j < G::GPW; ++j) {
+            const int n0 = (cw * G::GPW + j) * 8;
+            for (int lane = 0; lane < 32; ++lane)
+                for (int hh = 0; hh < 2; ++hh)
+                    for (int off = 0; off < D; off += 8) {
+                        const int g = lane >> 2, t = lane & 3;
+                        ywrites[ws_index<D>(n0 + 2 * t + hh, g + off)] += 1;
+                    }
+        }
+    for (int e = 0; e < G::TILE; ++e)
+        if (ywrites[e] != 1) return "forward Y' writes do not cover the tile once";
     return nullptr;
+}
+
+// The forward kernel's pipeline (rep_fwd_kernel): producer iteration k issues
+// the load of tile k + kFwdAhead (after waiting until at most kFwdStorePending
+// bulk stores are pending), gathers tile k and scatters + stores tile
+// k - kFwdLag. Replays the order for many tile counts and checks that every
+// load goes into a stage whose previous tile was already stored, and that the
+// stores still pending at that moment are all later tiles.
+static const char *check_forward_pipeline() {
+    for (int K = 1; K <= 64; ++K) {
+        std::vector<int> stored;  // tiles in store-issue order
+        std::vector<bool> issued(K, false);
+        for (int k = 0; k < K && k < kFwdAhead; ++k) issued[k] = true;  // prologue
+        for (int k = 0; k < K + kFwdLag; ++k) {
+            if (k < K) {
+                const int ahead = k + kFwdAhead;
+                if (ahead < K) {
+                    const int prev = ahead - kFwdStages;  // tile that last used the stage
+                    if (prev >= 0) {
+                        // wait_group.read kFwdStorePending: all but the newest kFwdStorePending stores are done
+                        int pos = -1;
+                        for (int i = 0; i < (int)stored.size(); ++i)
+                            if (stored[i] == prev) pos = i;
+                        if (pos < 0) return "stage reloaded before its store was issued";
+                        if ((int)stored.size() - pos <= kFwdStorePending)
+                            return "stage reloaded while its store may still read it";
+                    }
+                    issued[ahead] = true;
+                }
+                if (!issued[k]) return "tile gathered before its load was issued";
+            }
+            const int j = k - kFwdLag;
+            if (j >= 0 && j < K) stored.push_back(j);
+        }
+        if ((int)stored.size() != K) return "not every tile stored";
+    }
+    return nullptr;
+}
+
+// Inverse butterfly of the forward kernel's scatter: from a group's kept
+// entries back to its blades, y_t = in_sign_t * (1/S) * sum_f H[t][f] out_sign_f Y_f.
+static bool check_scatter(const RepDevice &dev, const double *x, const double *Xp) {
+    const int D = dev.D, S = dev.S;
+    for (int L = 0; L < (D == 8 ? 16 : D); ++L) {
+        const int m = L % D;
+        double v[8];
+        for (int f = 0; f < S; ++f) {
+            const int r = dev.ws_out_row[L][f];
+            const double e = Xp[r * D + dev.grp_col[m][r]];
+            v[f] = ((dev.ws_out_neg[L] >> f) & 1) ? -e : e;
+        }
+        for (int hs = 1; hs < S; hs <<= 1)
+            for (int a = 0; a < S; ++a)
+                if (!(a & hs)) {
+                    const double u = v[a], w = v[a | hs];
+                    v[a] = u + w;
+                    v[a | hs] = u - w;
+                }
+        for (int t = 0; t < S; ++t) {
+            const double got = (((dev.ws_in_neg[L] >> t) & 1) ? -v[t] : v[t]) * (1.0 / S);
+            if (std::fabs(got - x[dev.ws_blade[L][t]]) > 1e-12) return false;
+        }
+    }
+    return true;
 }
 
 static const char *check_ws(const RepDevice &dev) {
@@ -94,6 +173,10 @@ int main() {
     std::mt19937_64 rng(5);
     std::uniform_real_distribution<double> U(-1.0, 1.0);
     int cases = 0;
+    if (const char *why = check_forward_pipeline()) {
+        printf("FAIL forward pipeline: %s\n", why);
+        return 1;
+    }
     for (int n = 1; n <= 6; ++n) {
         for (int q = 0; q <= n; ++q) {
             int8_t sig[6] = {0};
@@ -193,6 +276,10 @@ int main() {
                 }
                 if (const char *why = check_ws(dev)) {
                     printf("FAIL ws layout n=%d q=%d side=%d: %s\n", n, q, side, why);
+                    return 1;
+                }
+                if (dev.ws_ready && !check_scatter(dev, x, Xp)) {
+                    printf("FAIL forward scatter n=%d q=%d side=%d\n", n, q, side);
                     return 1;
                 }
                 printf("n=%d q=%d side=%d D=%d S=%d err=%.1e\n", n, q, side, D, S, err);
