@@ -49,7 +49,7 @@ def parse():
     p.add_argument("--batch-log2", type=int, default=22, help="per-GPU batch = 2^k (22 is the headline shape)")
     p.add_argument("--negative", type=int, default=0, help="q of Cl(6-q, q); 0 = Cl(6,0)")
     p.add_argument("--no-extras", action="store_true", help="skip e2e, Cl(3,3) and cpu_baseline legs")
-    p.add_argument("--leg", choices=["train", "pairwise-f32", "v8-graph", "forward"], default="train",
+    p.add_argument("--leg", choices=["train", "pairwise-f32", "v8-graph", "forward", "operators"], default="train",
                    help="pairwise-f32: run only the float32 pairwise sweep (for profiling)")
     p.add_argument("--pairwise-log2", type=int, default=26, help="batch 2^k of the float32 pairwise sweep")
     p.add_argument("--algorithm", choices=["auto", "cayley", "representation"], default="auto",
@@ -441,6 +441,82 @@ def pairwise_f32_leg(lib, args, world) -> dict:
             "hbm_frac": gbs / hbm_peak, "flops_per_product": 2 * 32 * 64}
 
 
+# Measured FP64 peaks on this pool's B200 (148 x 8 warps of independent FMA /
+# MMA chains, CUDA events; the FMA and tensor paths share the FP64 units).
+FP64_DFMA_TFLOPS = 33.6
+FP64_DMMA_TFLOPS = 37.1
+
+
+def _time_launches(call, world, reps=10, warm=3) -> float:
+    """Average device milliseconds of `call` (CUDA events on the current stream), max over ranks."""
+    import torch
+
+    stream = torch.cuda.current_stream()
+    for _ in range(warm):
+        assert call() == 0
+    torch.cuda.synchronize()
+    barrier(world)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(reps):
+        assert call() == 0
+    e.record(stream)
+    torch.cuda.synchronize()
+    return max_over_ranks(s.elapsed_time(e) / reps, world)
+
+
+def operator_legs(lib, X, world) -> dict:
+    """The per-element operator paths at Cl(6,0), float64, on 2^22 elements (x resident,
+    2 GiB per operand, far above L2): sparse fixed-multivector plans (reference
+    geo_operator_apply_f64) and pairwise products with both operands varying
+    (reference geo_operator_gp_f64)."""
+    import torch
+
+    from geometricelementaryoperators_b200 import abi
+
+    batch = X.shape[0]
+    sig = abi.sig_array([1] * 6)
+    sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    Y = torch.empty_like(X)
+    xp, yp = ctypes.c_void_p(X.data_ptr()), ctypes.c_void_p(Y.data_ptr())
+    hbm_peak, _ = peaks()
+    out = {}
+    # Sparse plans: one fixed blade (a signed permutation, pure streaming) and the
+    # 32-term even-grade multivector with coefficients 1..32 (both on the right).
+    plans = {}
+    p1 = abi.OperatorPlanI32()
+    assert lib.geo_operator_plan_fixed_blade_i32(ctypes.byref(p1), 6, sig, 0, 0b000011, 3) == 0
+    plans["fixed_blade_e12"] = (p1, 1)
+    terms = (abi.OperatorTermI32 * 32)()
+    evens = [b for b in range(64) if bin(b).count("1") % 2 == 0]
+    for i, b in enumerate(evens):
+        terms[i].blade, terms[i].coefficient = b, i + 1
+    p32 = abi.OperatorPlanI32()
+    assert lib.geo_operator_plan_sparse_i32(ctypes.byref(p32), 6, sig, 0, terms, 32) == 0
+    plans["sparse_even_32_terms"] = (p32, 32)
+    for name, (plan, nterms) in plans.items():
+        ms = _time_launches(lambda: lib.geo_b200_sparse_apply_f64(ctypes.byref(plan), xp, yp, batch, sp), world)
+        gbs = batch * 1024 / (ms / 1e3) / 1e9
+        out["sparse_" + name] = {"value": batch * world / (ms / 1e3), "unit": "products/s", "ms_per_launch": ms,
+                                 "bytes_per_product": 1024, "flops_per_product": 2 * 64 * nterms,
+                                 "achieved_gbs": gbs, "hbm_frac": gbs / hbm_peak}
+    # Pairwise: y[s] = a[s] * b[s], 8192 flops and 1536 B per product.
+    Bm = torch.empty_like(X).copy_(X.flip(0))
+    bp = ctypes.c_void_p(Bm.data_ptr())
+    ms = _time_launches(lambda: lib.geo_b200_pairwise_gp_f64(6, sig, xp, bp, yp, batch, sp), world)
+    gbs = batch * 1536 / (ms / 1e3) / 1e9
+    tf = batch * 8192 / (ms / 1e3) / 1e12
+    out["pairwise_f64"] = {"value": batch * world / (ms / 1e3), "unit": "products/s", "ms_per_launch": ms,
+                           "bytes_per_product": 1536, "flops_per_product": 8192, "achieved_gbs": gbs,
+                           "hbm_frac": gbs / hbm_peak, "fp64_tflops": tf, "fp64_frac": tf / FP64_DFMA_TFLOPS}
+    del Y, Bm
+    torch.cuda.empty_cache()
+    out["workload"] = ("Cl(6,0) per-element operators, float64, 2^%d elements per GPU (operands resident, "
+                       "2 GiB each, no flush needed)" % int(math.log2(batch)))
+    out["fp64_peak"] = f"{FP64_DFMA_TFLOPS} TFLOP/s (measured DFMA rate on this pool's B200)"
+    return out
+
+
 def forward_leg(lib, X, q, world) -> dict:
     """Fixed-parameter forward y = x*W, Cl(6-q,q), float64, on the batch already
     resident for the training step (2 GiB of x read, 2 GiB of y written per
@@ -603,6 +679,7 @@ def run_b200(args, world, rank, local):
         extras["v8_graph"] = v8_graph_leg(args, world)
         # Fixed-parameter forward (multivector products/s) on the same resident batch.
         extras["forward"] = forward_leg(lib, X, q, world)
+        extras["operators"] = operator_legs(lib, X, world)
         # Same step on Cl(3,3) (the second signature of the headline config).
         X2, T2, w2 = X, T, w0
         tr33 = Trainer(lib, [1, 1, 1, -1, -1, -1], w2)
@@ -679,6 +756,8 @@ def run_b200(args, world, rank, local):
             line["v8_graph"] = extras["v8_graph"]
         if "forward" in extras:
             line["forward"] = extras["forward"]
+        if "operators" in extras:
+            line["operators"] = extras["operators"]
         if world == 1 and not args.no_extras:
             line["cpu_baseline"] = cpu_baseline_leg(q)
             line["v8_graph"]["cpu_baseline"] = v8_graph_reference_leg()
@@ -706,14 +785,16 @@ def main():
                     res["cpu_baseline"] = v8_graph_reference_leg()
                 print(json.dumps(res), flush=True)
             return
-        if args.leg == "forward":
+        if args.leg in ("forward", "operators"):
             import torch
 
             from geometricelementaryoperators_b200 import abi
 
             gen = torch.Generator(device="cuda").manual_seed(5)
             X = torch.rand((1 << args.batch_log2, 64), dtype=torch.float64, device="cuda", generator=gen)
-            res = forward_leg(abi.lib(), X.mul_(2).sub_(1), args.negative, world)
+            X.mul_(2).sub_(1)
+            res = (forward_leg(abi.lib(), X, args.negative, world) if args.leg == "forward"
+                   else operator_legs(abi.lib(), X, world))
             if rank == 0:
                 print(json.dumps(res), flush=True)
             return

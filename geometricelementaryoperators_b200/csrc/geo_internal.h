@@ -182,6 +182,19 @@ cudaError_t launch_rep_vjp(const RepDevice &rep, const double *inputs, const dou
 bool rep_forward_supported(const RepDevice &rep, const double *inputs, const double *outputs);
 cudaError_t launch_rep_forward(const RepDevice &rep, const double *inputs, const double *parameter, double *outputs,
                                size_t batch, cudaStream_t stream);
+// A parameter multivector given as a term list, W = sum_t value_t e_{blade[t]}
+// (repeated blades add up): value_t = coeff[t] when `values` is null, else
+// scale[t] * values[t] with `values` a device array of `terms` doubles.
+// Passed to kernels by value.
+struct TermParameter {
+    double coeff[64];
+    const double *values;
+    int8_t scale[64];
+    uint8_t blade[64];
+    int32_t terms;
+};
+cudaError_t launch_rep_forward_terms(const RepDevice &rep, const double *inputs, const TermParameter &parameter,
+                                     double *outputs, size_t batch, cudaStream_t stream);
 // Representation tables for (dimension, signature, side), built once and cached;
 // null when the algebra has no warp-specialised representation kernel (n < 5).
 const RepDevice *cached_rep_device(uint8_t dimension, const int8_t *signature, bool parameter_on_left);

@@ -791,8 +791,8 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 
 template <int D, int S>
 __global__ void __launch_bounds__(kWsThreads, 2)
-rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ W, size_t batch,
-               double *Y) {
+rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ W,
+               const TermParameter terms, size_t batch, double *Y) {
     using G = WsGeo<D, S>;
     constexpr int N = G::N, TS = G::TS, TILE = G::TILE;
     constexpr int kConsumers = kWsThreads - kWsProducers;
@@ -818,16 +818,27 @@ rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         s_gave_up = 0u;
     }
-    // W' = rho(W) (right) or rho(W)^T (left), as in rep_cycle_kernel.
+    // W' = rho(W) (right) or rho(W)^T (left), as in rep_cycle_kernel; W is a dense
+    // device array, or (W == null) the term list sum_t value_t e_{blade_t}.
     for (int idx = tid; idx < D * D; idx += kWsThreads) {
         const int k = idx / D, j = idx - k * D;
         const int col = rep.side ? k : j;
         double acc = 0.0;
-        for (int A = 0; A < N; ++A) {
-            if (rep.xm[A] != (k ^ j)) continue;
-            const double w = W[A];
-            const bool neg = (rep.sg[A] < 0) != ((__popc(rep.zm[A] & col) & 1) != 0);
-            acc += neg ? -w : w;
+        if (W != nullptr) {
+            for (int A = 0; A < N; ++A) {
+                if (rep.xm[A] != (k ^ j)) continue;
+                const double w = W[A];
+                const bool neg = (rep.sg[A] < 0) != ((__popc(rep.zm[A] & col) & 1) != 0);
+                acc += neg ? -w : w;
+            }
+        } else {
+            for (int t = 0; t < terms.terms; ++t) {
+                const int A = terms.blade[t];
+                if (rep.xm[A] != (k ^ j)) continue;
+                const double w = terms.values != nullptr ? terms.scale[t] * terms.values[t] : terms.coeff[t];
+                const bool neg = (rep.sg[A] < 0) != ((__popc(rep.zm[A] & col) & 1) != 0);
+                acc += neg ? -w : w;
+            }
         }
         Wp[idx] = acc;
     }
@@ -987,8 +998,8 @@ rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
 }
 
 template <int D, int S>
-cudaError_t launch_rep_fwd(const RepDevice &rep, const double *X, const double *W, double *Y, size_t batch,
-                           cudaStream_t stream) {
+cudaError_t launch_rep_fwd(const RepDevice &rep, const double *X, const double *W, const TermParameter &terms,
+                           double *Y, size_t batch, cudaStream_t stream) {
     using G = WsGeo<D, S>;
     if (rep.raw_stride != G::N || rep.D != D || rep.S != S) return cudaErrorInvalidValue;
     auto kernel = rep_fwd_kernel<D, S>;
@@ -1004,8 +1015,18 @@ cudaError_t launch_rep_fwd(const RepDevice &rep, const double *X, const double *
     size_t grid = (size_t)device_sm_count() * (size_t)per_sm;
     if (grid > tiles) grid = tiles;
     if (grid < 1) grid = 1;
-    kernel<<<(unsigned)grid, kWsThreads, smem, stream>>>(rep, X, W, batch, Y);
+    kernel<<<(unsigned)grid, kWsThreads, smem, stream>>>(rep, X, W, terms, batch, Y);
     return cudaGetLastError();
+}
+
+cudaError_t launch_rep_forward_impl(const RepDevice &rep, const double *X, const double *W,
+                                    const TermParameter &terms, double *Y, size_t batch, cudaStream_t stream) {
+    if (!rep_forward_supported(rep, X, Y)) return cudaErrorInvalidValue;
+    if (rep.D == 16 && rep.S == 4) return launch_rep_fwd<16, 4>(rep, X, W, terms, Y, batch, stream);
+    if (rep.D == 8 && rep.S == 8) return launch_rep_fwd<8, 8>(rep, X, W, terms, Y, batch, stream);
+    if (rep.D == 8 && rep.S == 4) return launch_rep_fwd<8, 4>(rep, X, W, terms, Y, batch, stream);
+    if (rep.D == 16 && rep.S == 2) return launch_rep_fwd<16, 2>(rep, X, W, terms, Y, batch, stream);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace
@@ -1016,12 +1037,17 @@ bool rep_forward_supported(const RepDevice &rep, const double *X, const double *
 
 cudaError_t launch_rep_forward(const RepDevice &rep, const double *X, const double *W, double *Y, size_t batch,
                                cudaStream_t stream) {
-    if (!rep_forward_supported(rep, X, Y)) return cudaErrorInvalidValue;
-    if (rep.D == 16 && rep.S == 4) return launch_rep_fwd<16, 4>(rep, X, W, Y, batch, stream);
-    if (rep.D == 8 && rep.S == 8) return launch_rep_fwd<8, 8>(rep, X, W, Y, batch, stream);
-    if (rep.D == 8 && rep.S == 4) return launch_rep_fwd<8, 4>(rep, X, W, Y, batch, stream);
-    if (rep.D == 16 && rep.S == 2) return launch_rep_fwd<16, 2>(rep, X, W, Y, batch, stream);
-    return cudaErrorInvalidValue;
+    if (W == nullptr) return cudaErrorInvalidValue;
+    TermParameter none;
+    none.terms = 0;
+    none.values = nullptr;
+    return launch_rep_forward_impl(rep, X, W, none, Y, batch, stream);
+}
+
+cudaError_t launch_rep_forward_terms(const RepDevice &rep, const double *X, const TermParameter &terms, double *Y,
+                                     size_t batch, cudaStream_t stream) {
+    if (terms.terms < 1 || terms.terms > 64) return cudaErrorInvalidValue;
+    return launch_rep_forward_impl(rep, X, nullptr, terms, Y, batch, stream);
 }
 
 cudaError_t launch_rep_cycle(const RepDevice &rep, const double *X, const double *T, const double *W, size_t batch,

@@ -1,20 +1,15 @@
 // pairwise.cu -- per-element geometric products where both operands vary
-// (geo_b200_pairwise_*) and sparse fixed-multivector plans over a batch
-// (geo_b200_sparse_*).
+// (geo_b200_pairwise_*).
 //
 // Reference semantics batched here (reference tree file:line):
 //   geo_operator_gp_f64       src/operator_kernel.c:412-447
 //   geo_operator_gp_f64_jvp   src/operator_kernel.c:449-492
 //   geo_operator_gp_f64_vjp   src/operator_kernel.c:494-539
-//   geo_operator_apply_f64 / _parametric_f64 / their VJPs
-//                             src/operator_kernel.c:191-334
 //
 // Layout: sample-major [batch][2^n]. Each CTA stages a tile of samples into
 // shared memory with coalesced loads; one thread computes one output blade of
 // one sample, reading the sign of every term from a bit table (bit p of
-// neg[l] set when e_l e_p = -e_(l^p)). Sparse plans bake, per term t, the
-// mask of sources whose sign is negative, so the inner loop is one bit test
-// and one FMA per term.
+// neg[l] set when e_l e_p = -e_(l^p)).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -482,149 +477,6 @@ geo_b200_status_t launch_pairwise(uint8_t dimension, const int8_t *signature, co
     return from_cuda(cudaGetLastError());
 }
 
-// ---- sparse fixed-multivector plans ----------------------------------------
-
-struct SparsePlan {
-    uint64_t negmask[64];  // bit src set when the sign of (src, blade_t) on the plan's side is -1
-    double coeff[64];      // integer coefficients as doubles (ignored by parametric calls)
-    uint8_t blade[64];
-    int32_t terms;
-    int32_t blades;
-};
-
-bool make_sparse_plan(const geo_operator_plan_i32_t *p, SparsePlan *out) {
-    if (p == nullptr || p->abi_version != GEO_OPERATOR_ABI_VERSION || !geo::signature_valid(p->signature, p->dimension))
-        return false;
-    if (p->side != GEO_OPERATOR_SIDE_LEFT && p->side != GEO_OPERATOR_SIDE_RIGHT) return false;
-    if (p->kind != GEO_OPERATOR_PLAN_FIXED_BLADE && p->kind != GEO_OPERATOR_PLAN_SPARSE_FIXED_MULTIVECTOR) return false;
-    if (p->term_count == 0 || p->term_count > GEO_OPERATOR_MAX_TERMS) return false;
-    if (p->kind == GEO_OPERATOR_PLAN_FIXED_BLADE && p->term_count != 1) return false;
-    memset(out, 0, sizeof(*out));
-    const unsigned blades = 1u << p->dimension;
-    out->terms = p->term_count;
-    out->blades = (int32_t)blades;
-    for (unsigned t = 0; t < p->term_count; ++t) {
-        if (p->terms[t].blade >= blades || p->terms[t].coefficient == 0) return false;
-        out->blade[t] = p->terms[t].blade;
-        out->coeff[t] = (double)p->terms[t].coefficient;
-        uint64_t m = 0;
-        for (unsigned src = 0; src < blades; ++src) {
-            // reference src/operator_kernel.c:88-96: right side s(src, blade), left side s(blade, src)
-            const int s = p->side == GEO_OPERATOR_SIDE_RIGHT
-                              ? geo::sign_rule((uint8_t)src, p->terms[t].blade, p->signature, p->dimension)
-                              : geo::sign_rule(p->terms[t].blade, (uint8_t)src, p->signature, p->dimension);
-            if (s < 0) m |= (uint64_t)1 << src;
-        }
-        out->negmask[t] = m;
-    }
-    return true;
-}
-
-enum SparseMode : int { kSparseApply = 0, kSparseVjpInput = 1, kSparseParamVjp = 2 };
-
-// kSparseApply:    out[s][o]   = sum_t in[s][o^b_t] c_t sgn_t(o^b_t)
-// kSparseVjpInput: out[s][src] = sum_t cot[s][src^b_t] c_t sgn_t(src)
-// kSparseParamVjp: also records[cta][t] += sum_src cot[src^b_t] in[src] sgn_t(src)
-template <int MODE>
-__global__ void __launch_bounds__(kThreads)
-sparse_kernel(const SparsePlan plan, const double *__restrict__ params, const double *__restrict__ a,
-              const double *__restrict__ b, double *__restrict__ out, size_t batch, double *__restrict__ records) {
-    const int N = plan.blades;
-    const int per_pass = kThreads / N;
-    extern __shared__ __align__(16) double sm[];
-    double *As = sm;                    // per_pass * N  (input or cotangent)
-    double *Bs = As + per_pass * N;     // per_pass * N  (cotangent for the parameter VJP)
-    __shared__ double coeff[64];
-    __shared__ double pacc[kThreads];
-    if (threadIdx.x < plan.terms) coeff[threadIdx.x] = params != nullptr ? params[threadIdx.x] : plan.coeff[threadIdx.x];
-    const int s = threadIdx.x / N;
-    const int j = threadIdx.x - s * N;
-    const bool lane_ok = s < per_pass;
-    // Parameter-VJP accumulators: thread (s, j) accumulates term t = j (j < terms).
-    double pa = 0.0;
-    for (size_t first = (size_t)blockIdx.x * per_pass; first < batch; first += (size_t)gridDim.x * per_pass) {
-        __syncthreads();
-        stage(As, a, first, per_pass, N, batch);
-        if (MODE == kSparseParamVjp) stage(Bs, b, first, per_pass, N, batch);
-        __syncthreads();
-        const size_t sample = first + (size_t)s;
-        if (!lane_ok || sample >= batch) continue;
-        const double *row = As + s * N;
-        if (MODE == kSparseApply) {
-            double acc = 0.0;
-            for (int t = 0; t < plan.terms; ++t) {
-                const int src = j ^ plan.blade[t];
-                acc = fma(row[src], apply_sign(coeff[t], (plan.negmask[t] >> src) & 1ull), acc);
-            }
-            out[sample * N + j] = acc;
-        } else {
-            // row = cotangent (VJP input) / input (param VJP uses Bs as cotangent)
-            const double *cot = MODE == kSparseVjpInput ? row : Bs + s * N;
-            if (out != nullptr) {
-                double acc = 0.0;
-                for (int t = 0; t < plan.terms; ++t)
-                    acc = fma(cot[j ^ plan.blade[t]], apply_sign(coeff[t], (plan.negmask[t] >> j) & 1ull), acc);
-                out[sample * N + j] = acc;
-            }
-            if (MODE == kSparseParamVjp && j < plan.terms) {
-                const uint64_t m = plan.negmask[j];
-                const int bt = plan.blade[j];
-                double acc = 0.0;
-                for (int src = 0; src < N; ++src)
-                    acc = fma(apply_sign(cot[src ^ bt], (m >> src) & 1ull), row[src], acc);
-                pa += acc;
-            }
-        }
-    }
-    if (MODE != kSparseParamVjp) return;
-    // Per-CTA record: sum over the sample slots of each term, in slot order.
-    pacc[threadIdx.x] = pa;
-    __syncthreads();
-    if (threadIdx.x < plan.terms) {
-        double acc = 0.0;
-        for (int ss = 0; ss < per_pass; ++ss) acc += pacc[ss * N + threadIdx.x];
-        records[(size_t)blockIdx.x * geo::kRecStride + threadIdx.x] = acc;
-    } else if (threadIdx.x < geo::kRecStride) {
-        records[(size_t)blockIdx.x * geo::kRecStride + threadIdx.x] = 0.0;
-    }
-}
-
-__global__ void copy_prefix_kernel(const double *__restrict__ src, double *__restrict__ dst, int count) {
-    if (threadIdx.x < count) dst[threadIdx.x] = src[threadIdx.x];
-}
-
-template <int MODE>
-geo_b200_status_t launch_sparse(const geo_operator_plan_i32_t *p, const double *params, const double *a,
-                                const double *b, double *out, double *param_out, size_t batch, cudaStream_t stream) {
-    SparsePlan plan;
-    if (!make_sparse_plan(p, &plan) || a == nullptr || batch == 0) return GEO_B200_INVALID_ARGUMENT;
-    const int N = plan.blades;
-    const int per_pass = kThreads / N;
-    size_t grid = (batch + per_pass - 1) / per_pass;
-    const size_t cap = (size_t)geo::device_sm_count() * 4;
-    if (grid > cap) grid = cap;
-    if (grid > (size_t)geo::kMaxCtas) grid = geo::kMaxCtas;
-    const size_t smem = (size_t)2 * per_pass * N * sizeof(double);
-    if (MODE != kSparseParamVjp) {
-        sparse_kernel<MODE><<<(unsigned)grid, kThreads, smem, stream>>>(plan, params, a, b, out, batch, nullptr);
-        return from_cuda(cudaGetLastError());
-    }
-    // Stream-ordered scratch for the per-CTA records (pool-cached after first use).
-    double *records = nullptr;
-    const size_t bytes = (grid + 1) * geo::kRecStride * sizeof(double);
-    cudaError_t e = cudaMallocAsync((void **)&records, bytes, stream);
-    if (e != cudaSuccess) return from_cuda(e);
-    sparse_kernel<MODE><<<(unsigned)grid, kThreads, smem, stream>>>(plan, params, a, b, out, batch, records);
-    e = cudaGetLastError();
-    if (e == cudaSuccess) e = geo::launch_reduce_records(records, (int)grid, records + grid * geo::kRecStride, stream);
-    if (e == cudaSuccess) {
-        copy_prefix_kernel<<<1, 64, 0, stream>>>(records + grid * geo::kRecStride, param_out, plan.terms);
-        e = cudaGetLastError();
-    }
-    cudaFreeAsync(records, stream);
-    return from_cuda(e);
-}
-
 }  // namespace
 
 extern "C" geo_b200_status_t geo_b200_pairwise_gp_f64(uint8_t dimension, const int8_t *signature,
@@ -673,38 +525,4 @@ extern "C" geo_b200_status_t geo_b200_pairwise_gp_f32(uint8_t dimension, const i
     }
     return launch_pairwise<float, kPairForward>(dimension, signature, device_left, left_even_compact != 0,
                                                 device_right, nullptr, nullptr, device_out, nullptr, batch, stream);
-}
-
-extern "C" geo_b200_status_t geo_b200_sparse_apply_f64(const geo_operator_plan_i32_t *plan, const double *device_in,
-                                                       double *device_out, size_t batch, cudaStream_t stream) {
-    if (device_out == nullptr) return GEO_B200_INVALID_ARGUMENT;
-    return launch_sparse<kSparseApply>(plan, nullptr, device_in, nullptr, device_out, nullptr, batch, stream);
-}
-
-extern "C" geo_b200_status_t geo_b200_sparse_apply_parametric_f64(const geo_operator_plan_i32_t *plan,
-                                                                  const double *device_parameters,
-                                                                  const double *device_in, double *device_out,
-                                                                  size_t batch, cudaStream_t stream) {
-    if (device_out == nullptr || device_parameters == nullptr) return GEO_B200_INVALID_ARGUMENT;
-    return launch_sparse<kSparseApply>(plan, device_parameters, device_in, nullptr, device_out, nullptr, batch,
-                                       stream);
-}
-
-extern "C" geo_b200_status_t geo_b200_sparse_apply_vjp_f64(const geo_operator_plan_i32_t *plan,
-                                                           const double *device_out_cotangent,
-                                                           double *device_in_cotangent, size_t batch,
-                                                           cudaStream_t stream) {
-    if (device_in_cotangent == nullptr) return GEO_B200_INVALID_ARGUMENT;
-    return launch_sparse<kSparseVjpInput>(plan, nullptr, device_out_cotangent, nullptr, device_in_cotangent, nullptr,
-                                          batch, stream);
-}
-
-extern "C" geo_b200_status_t geo_b200_sparse_apply_parametric_vjp_f64(
-    const geo_operator_plan_i32_t *plan, const double *device_parameters, const double *device_in,
-    const double *device_out_cotangent, double *device_in_cotangent, double *device_parameter_cotangent,
-    size_t batch, cudaStream_t stream) {
-    if (device_parameters == nullptr || device_out_cotangent == nullptr || device_parameter_cotangent == nullptr)
-        return GEO_B200_INVALID_ARGUMENT;
-    return launch_sparse<kSparseParamVjp>(plan, device_parameters, device_in, device_out_cotangent,
-                                          device_in_cotangent, device_parameter_cotangent, batch, stream);
 }
