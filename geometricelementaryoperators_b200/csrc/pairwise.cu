@@ -6,10 +6,11 @@
 //   geo_operator_gp_f64_jvp   src/operator_kernel.c:449-492
 //   geo_operator_gp_f64_vjp   src/operator_kernel.c:494-539
 //
-// Layout: sample-major [batch][2^n]. Each CTA stages a tile of samples into
-// shared memory with coalesced loads; one thread computes one output blade of
-// one sample, reading the sign of every term from a bit table (bit p of
-// neg[l] set when e_l e_p = -e_(l^p)).
+// Layout: sample-major [batch][2^n]. The generic kernel stages a tile of
+// samples into shared memory with coalesced loads; one thread computes one
+// output blade of one sample, reading the sign of every term from a bit table
+// (bit p of neg[l] set when e_l e_p = -e_(l^p)). The n = 6 forwards (float64
+// and float32) have dedicated TMA-staged kernels with compile-time signs.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -458,6 +459,265 @@ bool launch_pairwise_f32_fast(const int8_t *signature, const float *left, int co
     return true;
 }
 
+// ---- float64 n = 6, TMA-staged, compile-time signs --------------------------
+// y_o = sum_l a_l b_{l^o} sigma(l, o), sigma(l, o) = s(l, l^o). The sign rule
+// is a bilinear form over GF(2): s(l, m) = (-1)^(l^T M m) with
+// M = (strictly lower ones) + diag(negative axes). Splitting blade indices into
+// the high axes 4, 5 (block L0, O0 in 0..3) and the low axes 0..3 (i, k in
+// 0..15), sigma((L0,i), (O0,k)) = alpha_{L0,O0}(i) beta_{L0,O0}(k) gamma(i, k)
+// with gamma(i, k) = s_low(i, k), the sign rule of the low four axes alone. So
+// per 16 x 16 block (L0, O0) the 256 terms have compile-time signs gamma (one
+// DFMA with a free negation each); alpha flips the sign bits of the 16 a
+// values and beta is applied by flipping the accumulators' sign bits before
+// and after the block (exact). The host derives alpha and beta from the sign
+// rule and verifies the factorisation for every (l, o) before launching.
+//
+// CTA of 4 compute warps and one producer warp on tiles of 32 pairs
+// (lane = pair): compute warp w produces output blades 16w..16w+15 of the
+// tile's pairs. Operands arrive by TMA in [32][16] float64 boxes with the
+// 128-byte swizzle (one 16-byte read per lane hits a distinct bank group per
+// quarter warp) into a 2-stage ring: `full` mbarriers carry the transaction
+// bytes, `empty` mbarriers (one arrival per compute warp) release a stage to
+// the producer, so compute warps never wait for one another. Each compute
+// warp writes its outputs into its own swizzled box and stores it by TMA.
+constexpr int kF64Rows = 32;
+constexpr int kF64Compute = 4;                 // compute warps
+constexpr int kF64Threads = 32 * (kF64Compute + 1);
+constexpr int kF64Box = kF64Rows * 16;         // doubles of one [32][16] box (4 KB)
+constexpr int kF64Stages = 2;
+constexpr int kF64StageBoxes = 8;              // a: 4 boxes, b: 4 boxes
+// + 1024 bytes to align the boxes to the 1024-byte period of the 128-byte swizzle
+constexpr size_t kF64Smem = ((size_t)kF64Stages * kF64StageBoxes + kF64Compute) * kF64Box * sizeof(double) + 1024;
+
+struct F64BlockSigns {
+    uint16_t alpha[4][4];  // [L0][O0] bit i: a_{16 L0 + i} enters block (L0, O0) negated
+    uint16_t beta[4][4];   // [L0][O0] bit k: block (L0, O0) adds to y_{16 O0 + k} negated
+};
+
+// Sign of e_i e_k over axes 0..3 with negative-metric mask NEG (bit a: axis a negative).
+__host__ __device__ constexpr int low_sign(int i, int k, int neg) {
+    int s = 1;
+    for (int a = 0; a < 4; ++a) {
+        if ((i >> a) & 1) {
+            int lower = k & ((1 << a) - 1), c = 0;
+            for (; lower; lower &= lower - 1) ++c;
+            if (c & 1) s = -s;
+            if (((k >> a) & 1) && ((neg >> a) & 1)) s = -s;
+        }
+    }
+    return s;
+}
+
+// acc[k] += sum_i gamma(i, k) a[i] b[i ^ k] with compile-time indices and signs.
+template <int NEG, int I>
+__device__ __forceinline__ void f64_block_term(const double (&a)[16], const double (&b)[16], double (&acc)[16]) {
+    constexpr int i = I / 16, k = I % 16;
+    constexpr int sg = low_sign(i, k, NEG);
+    acc[k] = fma(sg > 0 ? a[i] : -a[i], b[i ^ k], acc[k]);
+}
+template <int NEG, int... I>
+__device__ __forceinline__ void f64_block(const double (&a)[16], const double (&b)[16], double (&acc)[16],
+                                          std::integer_sequence<int, I...>) {
+    (f64_block_term<NEG, I>(a, b, acc), ...);
+}
+
+__device__ __forceinline__ double flip_bit(double v, unsigned bit) {
+    return __hiloint2double(__double2hiint(v) ^ (int)(bit << 31), __double2loint(v));
+}
+
+// Double offset of (row, 16-byte chunk j) in a [32][16] float64 box with the 128-byte swizzle.
+__device__ __forceinline__ int sw128d(int row, int chunk) { return row * 16 + ((chunk ^ (row & 7)) << 1); }
+
+// Bounded wait for phase `parity` of an mbarrier; counts a give-up.
+__device__ __forceinline__ void f64_wait(uint64_t *bar, unsigned parity) {
+    const unsigned a = smem_u32(bar);
+    for (uint32_t i = 0; i < kTmaWaitLimit; ++i) {
+        unsigned done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return;
+    }
+    atomicAdd(&g_pairwise_tma_wait_failures, 1u);
+}
+
+template <int NEG>
+__global__ void __launch_bounds__(kF64Threads, 2)
+pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                           const __grid_constant__ CUtensorMap map_out, const F64BlockSigns signs, size_t batch) {
+    extern __shared__ unsigned char f64_raw[];
+    __shared__ __align__(8) uint64_t full[kF64Stages], empty[kF64Stages];
+    double *base = reinterpret_cast<double *>(((uintptr_t)f64_raw + 1023) & ~(uintptr_t)1023);
+    double *outbox = base + kF64Stages * kF64StageBoxes * kF64Box;  // one box per compute warp
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t tiles = (batch + kF64Rows - 1) / kF64Rows;
+    const int K = (size_t)blockIdx.x < tiles ? (int)((tiles - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+    if (tid == 0) {
+        for (int s = 0; s < kF64Stages; ++s) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_u32(&full[s])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(&empty[s])), "r"(kF64Compute)
+                         : "memory");
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    __syncthreads();
+    if (warp == kF64Compute) {
+        // ---- producer: one thread keeps the ring full
+        if (lane == 0) {
+            for (int k = 0; k < K; ++k) {
+                const int s = k % kF64Stages;
+                // the stage last held tile k - kF64Stages: wait until all compute warps released it
+                if (k >= kF64Stages) f64_wait(&empty[s], (unsigned)((k / kF64Stages - 1) & 1));
+                double *st = base + s * kF64StageBoxes * kF64Box;
+                const int y = (int)((blockIdx.x + (size_t)k * gridDim.x) * kF64Rows);
+                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(&full[s])),
+                             "r"((unsigned)(kF64StageBoxes * kF64Box * sizeof(double)))
+                             : "memory");
+                for (int c = 0; c < 4; ++c) {
+                    tma_load_2d(st + c * kF64Box, &map_a, 16 * c, y, &full[s]);
+                    tma_load_2d(st + (4 + c) * kF64Box, &map_b, 16 * c, y, &full[s]);
+                }
+            }
+        }
+        return;
+    }
+    // ---- compute warps
+    double *ob = outbox + warp * kF64Box;
+    for (int k = 0; k < K; ++k) {
+        const int s = k % kF64Stages;
+        f64_wait(&full[s], (unsigned)((k / kF64Stages) & 1));
+        const double *A = base + s * kF64StageBoxes * kF64Box;
+        const double *Bm = A + 4 * kF64Box;
+        double acc[16];
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) acc[kk] = 0.0;
+        unsigned prev = 0u;
+#pragma unroll
+        for (int L0 = 0; L0 < 4; ++L0) {
+            const unsigned am = signs.alpha[L0][warp], bm = signs.beta[L0][warp];
+            double av[16], bv[16];
+            const double *ab = A + L0 * kF64Box;
+            const double *bb = Bm + (L0 ^ warp) * kF64Box;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const double2 u = *reinterpret_cast<const double2 *>(&ab[sw128d(lane, j)]);
+                const double2 v = *reinterpret_cast<const double2 *>(&bb[sw128d(lane, j)]);
+                av[2 * j] = u.x; av[2 * j + 1] = u.y;
+                bv[2 * j] = v.x; bv[2 * j + 1] = v.y;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) av[i] = flip_bit(av[i], (am >> i) & 1u);
+            const unsigned fm = bm ^ prev;
+#pragma unroll
+            for (int kk = 0; kk < 16; ++kk) acc[kk] = flip_bit(acc[kk], (fm >> kk) & 1u);
+            prev = bm;
+            f64_block<NEG>(av, bv, acc, std::make_integer_sequence<int, 256>{});
+        }
+        // The warp is done reading stage s.
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(&empty[s])) : "memory");
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) acc[kk] = flip_bit(acc[kk], (prev >> kk) & 1u);
+        // The store of tile k - 1 from this warp's box must have finished reading it.
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<double2 *>(&ob[sw128d(lane, j)]) = make_double2(acc[2 * j], acc[2 * j + 1]);
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+            const int row = (int)((blockIdx.x + (size_t)k * gridDim.x) * kF64Rows);
+            tma_store_2d(&map_out, 16 * warp, row, ob);
+            asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+        }
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+}
+
+// [rows][64] float64 tensor, [32][16] boxes, 128-byte swizzle, zero fill.
+bool encode_rows_f64(CUtensorMap *map, const double *ptr, size_t rows) {
+    const auto encode = tensor_map_encoder();
+    if (encode == nullptr || rows == 0 || rows > 0xffffffffull) return false;
+    const cuuint64_t dims[2] = {64, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {64 * sizeof(double)};
+    const cuuint32_t box[2] = {16, (cuuint32_t)kF64Rows};
+    const cuuint32_t elem[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, const_cast<double *>(ptr), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// alpha / beta of the block factorisation for a 6-dimensional signature;
+// false (use the generic kernel) if sigma does not factor as alpha beta gamma.
+bool f64_block_signs(const geo::SignPlan &plan, int neg_low, F64BlockSigns *out) {
+    // plan.neg[l] bit p: s(l, p) = -1 (parameter-on-right plan: sigma(i, p) = s(i, p)).
+    auto sigma = [&](int l, int o) { return ((plan.neg[l] >> (l ^ o)) & 1ull) ? -1 : 1; };
+    for (int L0 = 0; L0 < 4; ++L0)
+        for (int O0 = 0; O0 < 4; ++O0) {
+            int alpha[16], beta[16];
+            for (int i = 0; i < 16; ++i) alpha[i] = sigma(16 * L0 + i, 16 * O0);
+            for (int k = 0; k < 16; ++k) beta[k] = sigma(16 * L0, 16 * O0 + k) * alpha[0];
+            uint16_t am = 0, bm = 0;
+            for (int i = 0; i < 16; ++i) {
+                if (alpha[i] < 0) am |= (uint16_t)(1u << i);
+                for (int k = 0; k < 16; ++k)
+                    if (sigma(16 * L0 + i, 16 * O0 + k) != alpha[i] * beta[k] * low_sign(i, k, neg_low)) return false;
+            }
+            for (int k = 0; k < 16; ++k)
+                if (beta[k] < 0) bm |= (uint16_t)(1u << k);
+            out->alpha[L0][O0] = am;
+            out->beta[L0][O0] = bm;
+        }
+    return true;
+}
+
+template <int NEG>
+cudaError_t launch_f64_tma_neg(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mo,
+                               const F64BlockSigns &signs, size_t batch, cudaStream_t stream) {
+    auto kernel = pairwise_f64_n6_tma_kernel<NEG>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kF64Smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kF64Threads, kF64Smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    const size_t tiles = (batch + kF64Rows - 1) / kF64Rows;
+    size_t grid = (size_t)geo::device_sm_count() * (size_t)per_sm;
+    if (grid > tiles) grid = tiles;
+    kernel<<<(unsigned)grid, kF64Threads, kF64Smem, stream>>>(ma, mb, mo, signs, batch);
+    return cudaGetLastError();
+}
+
+template <int... NEG>
+cudaError_t launch_f64_tma_dispatch(int neg, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mo,
+                                    const F64BlockSigns &signs, size_t batch, cudaStream_t stream,
+                                    std::integer_sequence<int, NEG...>) {
+    cudaError_t e = cudaErrorInvalidValue;
+    ((neg == NEG ? (e = launch_f64_tma_neg<NEG>(ma, mb, mo, signs, batch, stream), true) : false) || ...);
+    return e;
+}
+
+// float64 n = 6 forward on the TMA kernel; false when it does not apply
+// (unaligned operands, no tensor-map encoder, sign table that does not factor).
+bool launch_pairwise_f64_fast(const geo::SignPlan &plan, const int8_t *signature, const double *left,
+                              const double *right, double *out, size_t batch, cudaStream_t stream, cudaError_t *err) {
+    if (plan.blades != 64 || ((uintptr_t)left | (uintptr_t)right | (uintptr_t)out) & 15u) return false;
+    int neg_low = 0;
+    for (int a = 0; a < 4; ++a)
+        if (signature[a] < 0) neg_low |= 1 << a;
+    F64BlockSigns signs;
+    if (!f64_block_signs(plan, neg_low, &signs)) return false;
+    CUtensorMap ma, mb, mo;
+    if (!encode_rows_f64(&ma, left, batch) || !encode_rows_f64(&mb, right, batch) || !encode_rows_f64(&mo, out, batch))
+        return false;
+    *err = launch_f64_tma_dispatch(neg_low, ma, mb, mo, signs, batch, stream, std::make_integer_sequence<int, 16>{});
+    return true;
+}
+
 template <typename T, int MODE>
 geo_b200_status_t launch_pairwise(uint8_t dimension, const int8_t *signature, const T *left, int left_compact,
                                   const T *right, const T *aux0, const T *aux1, T *out0, T *out1, size_t batch,
@@ -483,6 +743,13 @@ extern "C" geo_b200_status_t geo_b200_pairwise_gp_f64(uint8_t dimension, const i
                                                       const double *device_left, const double *device_right,
                                                       double *device_out, size_t batch, cudaStream_t stream) {
     if (device_out == nullptr) return GEO_B200_INVALID_ARGUMENT;
+    if (dimension == 6 && device_left != nullptr && device_right != nullptr && batch > 0) {
+        const geo::SignPlan *plan = geo::cached_sign_plan(6, signature, 0);
+        cudaError_t e = cudaSuccess;
+        if (plan != nullptr && launch_pairwise_f64_fast(*plan, signature, device_left, device_right, device_out,
+                                                        batch, stream, &e))
+            return from_cuda(e);
+    }
     return launch_pairwise<double, kPairForward>(dimension, signature, device_left, 0, device_right, nullptr, nullptr,
                                                  device_out, nullptr, batch, stream);
 }

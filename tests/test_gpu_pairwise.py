@@ -36,6 +36,57 @@ def test_pairwise_f64_all_signatures(oracle):
         assert tol_close(host(jt), jv, TOL)
 
 
+def test_pairwise_f64_n6_tma_path(oracle):
+    """n = 6 float64 forward on the TMA kernel (16-byte aligned operands): every
+    canonical signature plus non-canonical ones (the kernel is specialised on the
+    metric of axes 0..3), a batch ending inside a 32-row tile (rows past it stay
+    untouched), and the 8-byte aligned fallback."""
+    import torch
+
+    L = abi.lib()
+    B = 1000 + 17
+    sigs = [canonical_signature(6, q) for q in range(7)] + [[-1, 1, -1, 1, 1, -1], [1, -1, 1, 1, -1, 1]]
+    for k, sig in enumerate(sigs):
+        a, b = splitmix_uniform(710 + k, (B, 64)), splitmix_uniform(720 + k, (B, 64))
+        da, db = dev(a), dev(b)
+        out = torch.full((B + 40, 64), 7.0, dtype=torch.float64, device="cuda")
+        assert L.geo_b200_pairwise_gp_f64(6, abi.sig_array(sig), ptr(da), ptr(db), ptr(out), B, stream()) == 0
+        sync()
+        want = np.stack([oracle.gp(sig, a[i], b[i]) for i in range(B)])
+        got = host(out)
+        assert tol_close(got[:B], want, TOL), (sig, max_violation(got[:B], want, TOL))
+        assert np.all(got[B:] == 7.0)
+        if k in (0, 3):
+            big = dev(np.concatenate([[0.0], a.ravel()]))
+            o8 = dev(np.zeros(a.size + 1))
+            assert L.geo_b200_pairwise_gp_f64(6, abi.sig_array(sig), ctypes.c_void_p(big.data_ptr() + 8), ptr(db),
+                                              ctypes.c_void_p(o8.data_ptr() + 8), B, stream()) == 0
+            sync()
+            assert tol_close(host(o8)[1:].reshape(B, 64), want, TOL)
+
+
+def test_pairwise_f64_full_size_spot_rows(oracle):
+    """2^22 + 9 pairs of Cl(6,0) (the operator bench shape with a ragged tail): spot rows,
+    first and last tiles included."""
+    import torch
+
+    L = abi.lib()
+    sig = canonical_signature(6, 0)
+    B = (1 << 22) + 9
+    gen = torch.Generator(device="cuda").manual_seed(8)
+    da = torch.rand((B, 64), dtype=torch.float64, device="cuda", generator=gen).mul_(2).sub_(1)
+    db = torch.rand((B, 64), dtype=torch.float64, device="cuda", generator=gen).mul_(2).sub_(1)
+    out = torch.empty_like(da)
+    assert L.geo_b200_pairwise_gp_f64(6, abi.sig_array(sig), ptr(da), ptr(db), ptr(out), B, stream()) == 0
+    sync()
+    rows = np.unique(np.concatenate([np.arange(40), np.arange(B - 40, B),
+                                     np.random.default_rng(4).integers(0, B, 300)]))
+    idx = torch.as_tensor(rows, device="cuda")
+    a, b, got = host(da[idx]), host(db[idx]), host(out[idx])
+    want = np.stack([oracle.gp(sig, a[i], b[i]) for i in range(len(rows))])
+    assert tol_close(got, want, TOL), max_violation(got, want, TOL)
+
+
 @pytest.mark.parametrize("q", [0, 3, 6])
 @pytest.mark.parametrize("compact", [0, 1])
 def test_pairwise_f32_even_operand(oracle, compact, q):
