@@ -509,10 +509,22 @@ def operator_legs(lib, X, world) -> dict:
     out["pairwise_f64"] = {"value": batch * world / (ms / 1e3), "unit": "products/s", "ms_per_launch": ms,
                            "bytes_per_product": 1536, "flops_per_product": 8192, "achieved_gbs": gbs,
                            "hbm_frac": gbs / hbm_peak, "fp64_tflops": tf, "fp64_frac": tf / FP64_DFMA_TFLOPS}
-    del Y, Bm
+    # Pairwise VJP: both cotangents (a_bar, b_bar) from y_bar; 16384 flops per product,
+    # 2560 algorithmic bytes (a, b, y_bar read once; a_bar, b_bar written).
+    Cb = torch.empty_like(X).copy_(X.roll(1, 0))
+    Z = torch.empty_like(X)
+    cp, zp = ctypes.c_void_p(Cb.data_ptr()), ctypes.c_void_p(Z.data_ptr())
+    ms = _time_launches(lambda: lib.geo_b200_pairwise_gp_vjp_f64(6, sig, xp, bp, cp, yp, zp, batch, sp), world)
+    tf = batch * 16384 / (ms / 1e3) / 1e12
+    gbs = batch * 2560 / (ms / 1e3) / 1e9
+    out["pairwise_f64_vjp"] = {"value": batch * world / (ms / 1e3), "unit": "products/s", "ms_per_launch": ms,
+                               "bytes_per_product": 2560, "flops_per_product": 16384, "achieved_gbs": gbs,
+                               "hbm_frac": gbs / hbm_peak, "fp64_tflops": tf, "fp64_frac": tf / FP64_DFMA_TFLOPS}
+    del Y, Bm, Cb, Z
     torch.cuda.empty_cache()
     out["workload"] = ("Cl(6,0) per-element operators, float64, 2^%d elements per GPU (operands resident, "
-                       "2 GiB each, no flush needed)" % int(math.log2(batch)))
+                       "%d MiB each, %s)" % (int(math.log2(batch)), batch * 512 >> 20,
+                                             "no flush needed" if batch * 512 > (256 << 20) else "small case"))
     out["fp64_peak"] = f"{FP64_DFMA_TFLOPS} TFLOP/s (measured DFMA rate on this pool's B200)"
     return out
 
@@ -565,7 +577,8 @@ def forward_leg(lib, X, q, world) -> dict:
     torch.cuda.empty_cache()
     best = out["representation"]
     return {"workload": f"Cl({6 - q},{q}) fixed-parameter forward y = x*W, float64, batch 2^{int(math.log2(batch))} "
-                        "per GPU (x resident, 2 GiB read + 2 GiB written per launch; no flush needed)",
+                        f"per GPU (x resident, {batch * 512 >> 20} MiB read + {batch * 512 >> 20} MiB written "
+                        "per launch)",
             "value": best["value"], "unit": "products/s", "bytes_per_product": FORWARD_BYTES_PER_SAMPLE,
             "roofline": {"bound": "hbm", "achieved": best["achieved_gbs"], "peak": hbm_peak, "unit": "GB/s",
                          "frac": best["hbm_frac"],

@@ -492,6 +492,7 @@ constexpr size_t kF64Smem = ((size_t)kF64Stages * kF64StageBoxes + kF64Compute) 
 struct F64BlockSigns {
     uint16_t alpha[4][4];  // [L0][O0] bit i: a_{16 L0 + i} enters block (L0, O0) negated
     uint16_t beta[4][4];   // [L0][O0] bit k: block (L0, O0) adds to y_{16 O0 + k} negated
+    uint16_t bflip[4];     // [L0 ^ O0] bit j: b_{16 (L0 ^ O0) + j} is negated on load (VJP operands)
 };
 
 // Sign of e_i e_k over axes 0..3 with negative-metric mask NEG (bit a: axis a negative).
@@ -549,6 +550,7 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
                            const __grid_constant__ CUtensorMap map_out, const F64BlockSigns signs, size_t batch) {
     extern __shared__ unsigned char f64_raw[];
     __shared__ __align__(8) uint64_t full[kF64Stages], empty[kF64Stages];
+    __shared__ F64BlockSigns sgn;
     double *base = reinterpret_cast<double *>(((uintptr_t)f64_raw + 1023) & ~(uintptr_t)1023);
     double *outbox = base + kF64Stages * kF64StageBoxes * kF64Box;  // one box per compute warp
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -561,6 +563,7 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
                          : "memory");
         }
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        sgn = signs;
     }
     __syncthreads();
     if (warp == kF64Compute) {
@@ -597,7 +600,7 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
         unsigned prev = 0u;
 #pragma unroll
         for (int L0 = 0; L0 < 4; ++L0) {
-            const unsigned am = signs.alpha[L0][warp], bm = signs.beta[L0][warp];
+            const unsigned am = sgn.alpha[L0][warp], bm = sgn.beta[L0][warp];
             double av[16], bv[16];
             const double *ab = A + L0 * kF64Box;
             const double *bb = Bm + (L0 ^ warp) * kF64Box;
@@ -610,6 +613,11 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
             }
 #pragma unroll
             for (int i = 0; i < 16; ++i) av[i] = flip_bit(av[i], (am >> i) & 1u);
+            const unsigned bf = sgn.bflip[L0 ^ warp];
+            if (bf != 0u) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) bv[j] = flip_bit(bv[j], (bf >> j) & 1u);
+            }
             const unsigned fm = bm ^ prev;
 #pragma unroll
             for (int kk = 0; kk < 16; ++kk) acc[kk] = flip_bit(acc[kk], (fm >> kk) & 1u);
@@ -653,9 +661,18 @@ bool encode_rows_f64(CUtensorMap *map, const double *ptr, size_t rows) {
 
 // alpha / beta of the block factorisation for a 6-dimensional signature;
 // false (use the generic kernel) if sigma does not factor as alpha beta gamma.
-bool f64_block_signs(const geo::SignPlan &plan, int neg_low, F64BlockSigns *out) {
+// rev_a / rev_b multiply operand blade m of a / b by s(m, m) (the operands of
+// the VJP products).
+bool f64_block_signs(const geo::SignPlan &plan, int neg_low, bool rev_a, bool rev_b, F64BlockSigns *out) {
     // plan.neg[l] bit p: s(l, p) = -1 (parameter-on-right plan: sigma(i, p) = s(i, p)).
     auto sigma = [&](int l, int o) { return ((plan.neg[l] >> (l ^ o)) & 1ull) ? -1 : 1; };
+    auto self_negative = [&](int m) { return ((plan.neg[m] >> m) & 1ull) != 0; };  // s(m, m) = -1
+    for (int c = 0; c < 4; ++c) {
+        uint16_t f = 0;
+        for (int j = 0; rev_b && j < 16; ++j)
+            if (self_negative(16 * c + j)) f |= (uint16_t)(1u << j);
+        out->bflip[c] = f;
+    }
     for (int L0 = 0; L0 < 4; ++L0)
         for (int O0 = 0; O0 < 4; ++O0) {
             int alpha[16], beta[16];
@@ -663,7 +680,7 @@ bool f64_block_signs(const geo::SignPlan &plan, int neg_low, F64BlockSigns *out)
             for (int k = 0; k < 16; ++k) beta[k] = sigma(16 * L0, 16 * O0 + k) * alpha[0];
             uint16_t am = 0, bm = 0;
             for (int i = 0; i < 16; ++i) {
-                if (alpha[i] < 0) am |= (uint16_t)(1u << i);
+                if ((alpha[i] < 0) != (rev_a && self_negative(16 * L0 + i))) am |= (uint16_t)(1u << i);
                 for (int k = 0; k < 16; ++k)
                     if (sigma(16 * L0 + i, 16 * O0 + k) != alpha[i] * beta[k] * low_sign(i, k, neg_low)) return false;
             }
@@ -704,13 +721,14 @@ cudaError_t launch_f64_tma_dispatch(int neg, const CUtensorMap &ma, const CUtens
 // float64 n = 6 forward on the TMA kernel; false when it does not apply
 // (unaligned operands, no tensor-map encoder, sign table that does not factor).
 bool launch_pairwise_f64_fast(const geo::SignPlan &plan, const int8_t *signature, const double *left,
-                              const double *right, double *out, size_t batch, cudaStream_t stream, cudaError_t *err) {
+                              const double *right, double *out, size_t batch, cudaStream_t stream, cudaError_t *err,
+                              bool rev_left = false, bool rev_right = false) {
     if (plan.blades != 64 || ((uintptr_t)left | (uintptr_t)right | (uintptr_t)out) & 15u) return false;
     int neg_low = 0;
     for (int a = 0; a < 4; ++a)
         if (signature[a] < 0) neg_low |= 1 << a;
     F64BlockSigns signs;
-    if (!f64_block_signs(plan, neg_low, &signs)) return false;
+    if (!f64_block_signs(plan, neg_low, rev_left, rev_right, &signs)) return false;
     CUtensorMap ma, mb, mo;
     if (!encode_rows_f64(&ma, left, batch) || !encode_rows_f64(&mb, right, batch) || !encode_rows_f64(&mo, out, batch))
         return false;
@@ -762,6 +780,24 @@ extern "C" geo_b200_status_t geo_b200_pairwise_gp_vjp_f64(uint8_t dimension, con
                                                           cudaStream_t stream) {
     if (device_out_cotangent == nullptr || (device_left_cotangent == nullptr && device_right_cotangent == nullptr))
         return GEO_B200_INVALID_ARGUMENT;
+    // n = 6: two forward products on the TMA kernel. With y = a b and
+    // m~ = s(m, m) m per blade (the transpose of multiplication by e_m is s(m, m)
+    // times itself): a_bar = y_bar b~ and b_bar = a~ y_bar.
+    const geo::SignPlan *plan = dimension == 6 ? geo::cached_sign_plan(6, signature, 0) : nullptr;
+    const bool al = ((uintptr_t)device_left | (uintptr_t)device_right | (uintptr_t)device_out_cotangent |
+                     (uintptr_t)device_left_cotangent | (uintptr_t)device_right_cotangent) % 16u == 0u;
+    if (plan != nullptr && al && device_left != nullptr && device_right != nullptr && batch > 0 &&
+        tensor_map_encoder() != nullptr) {
+        cudaError_t e = cudaSuccess;
+        bool ran = true;
+        if (device_left_cotangent != nullptr)
+            ran = launch_pairwise_f64_fast(*plan, signature, device_out_cotangent, device_right, device_left_cotangent,
+                                           batch, stream, &e, false, true);
+        if (ran && e == cudaSuccess && device_right_cotangent != nullptr)
+            ran = launch_pairwise_f64_fast(*plan, signature, device_left, device_out_cotangent,
+                                           device_right_cotangent, batch, stream, &e, true, false);
+        if (ran) return from_cuda(e);
+    }
     return launch_pairwise<double, kPairVjp>(dimension, signature, device_left, 0, device_right, device_out_cotangent,
                                              nullptr, device_left_cotangent, device_right_cotangent, batch, stream);
 }

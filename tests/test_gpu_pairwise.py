@@ -56,6 +56,22 @@ def test_pairwise_f64_n6_tma_path(oracle):
         got = host(out)
         assert tol_close(got[:B], want, TOL), (sig, max_violation(got[:B], want, TOL))
         assert np.all(got[B:] == 7.0)
+        # VJP: two forward products with sign-flipped operands; each output on its own too.
+        c = splitmix_uniform(730 + k, (B, 64))
+        vj = [oracle.gp_vjp(sig, a[i], b[i], c[i]) for i in range(B)]
+        want_l, want_r = np.stack([u for u, _ in vj]), np.stack([v for _, v in vj])
+        dc = dev(c)
+        for which in ("both", "left", "right"):
+            lb = dev(np.zeros((B, 64))) if which != "right" else None
+            rb = dev(np.zeros((B, 64))) if which != "left" else None
+            assert L.geo_b200_pairwise_gp_vjp_f64(6, abi.sig_array(sig), ptr(da), ptr(db), ptr(dc),
+                                                  ptr(lb) if lb is not None else None,
+                                                  ptr(rb) if rb is not None else None, B, stream()) == 0
+            sync()
+            if lb is not None:
+                assert tol_close(host(lb), want_l, TOL), (sig, which, max_violation(host(lb), want_l, TOL))
+            if rb is not None:
+                assert tol_close(host(rb), want_r, TOL), (sig, which, max_violation(host(rb), want_r, TOL))
         if k in (0, 3):
             big = dev(np.concatenate([[0.0], a.ravel()]))
             o8 = dev(np.zeros(a.size + 1))
