@@ -533,7 +533,8 @@ def forward_leg(lib, X, q, world) -> dict:
     """Fixed-parameter forward y = x*W, Cl(6-q,q), float64, on the batch already
     resident for the training step (2 GiB of x read, 2 GiB of y written per
     launch, far above L2): geo_b200_forward_f64 on the representation kernel,
-    and the device ABI's planned forward (Cayley kernel) beside it."""
+    the reference ABI's device calls a drop-in caller makes (planned forward and
+    the MSE-SGD step with residuals stored), and the Cayley kernel beside them."""
     import torch
 
     from geometricelementaryoperators_b200 import abi
@@ -549,11 +550,22 @@ def forward_leg(lib, X, q, world) -> dict:
     assert lib.geo_batch_gp_plan_init(ctypes.byref(plan), 6, abi.sig_array(sig)) == 0
     cplan = abi.CudaPlan()
     assert lib.geo_batch_gp_cuda_plan_upload(ctypes.byref(cplan), ctypes.byref(plan)) == 0
+    T = torch.empty_like(X).copy_(X.roll(3, 0))
+    R = torch.empty_like(X)
+    w2 = w.clone()
+    g = torch.empty(64, dtype=torch.float64, device="cuda")
+    loss = torch.empty(1, dtype=torch.float64, device="cuda")
+    tp, rp, w2p, gp, lp = (ctypes.c_void_p(t.data_ptr()) for t in (T, R, w2, g, loss))
     calls = {
         "representation": lambda: lib.geo_b200_forward_f64(6, abi.sig_array(sig), 0, 2, xp, wp, yp, batch, sp),
-        "cayley_device_abi": lambda: lib.geo_batch_gp_cuda_planned_forward_f64(ctypes.byref(cplan), xp, batch, wp,
-                                                                              0, yp, sp),
+        "device_abi_planned_forward": lambda: lib.geo_batch_gp_cuda_planned_forward_f64(ctypes.byref(cplan), xp,
+                                                                                       batch, wp, 0, yp, sp),
+        "cayley": lambda: lib.geo_b200_forward_f64(6, abi.sig_array(sig), 0, 1, xp, wp, yp, batch, sp),
+        # forward -> residual (stored) -> loss -> VJP -> SGD; 1536 algorithmic bytes per sample
+        "device_abi_mse_sgd_step": lambda: lib.geo_batch_gp_cuda_mse_sgd_step_f64(ctypes.byref(cplan), xp, tp, batch,
+                                                                                 1e-9, 0, w2p, rp, gp, lp, sp),
     }
+    bytes_per = {"device_abi_mse_sgd_step": 3 * 64 * 8}
     out = {}
     hbm_peak, _ = peaks()
     for name, call in calls.items():
@@ -569,11 +581,11 @@ def forward_leg(lib, X, q, world) -> dict:
         e.record(stream)
         torch.cuda.synchronize()
         ms = max_over_ranks(s.elapsed_time(e) / reps, world)
-        gbs = batch * FORWARD_BYTES_PER_SAMPLE / (ms / 1e3) / 1e9
-        out[name] = {"value": batch * world / (ms / 1e3), "unit": "products/s", "ms_per_launch": ms,
-                     "achieved_gbs": gbs, "hbm_frac": gbs / hbm_peak}
+        gbs = batch * bytes_per.get(name, FORWARD_BYTES_PER_SAMPLE) / (ms / 1e3) / 1e9
+        out[name] = {"value": batch * world / (ms / 1e3), "unit": "samples/s" if name in bytes_per else "products/s",
+                     "ms_per_call": ms, "achieved_gbs": gbs, "hbm_frac": gbs / hbm_peak}
     lib.geo_batch_gp_cuda_plan_destroy(ctypes.byref(cplan))
-    del Y
+    del Y, T, R
     torch.cuda.empty_cache()
     best = out["representation"]
     return {"workload": f"Cl({6 - q},{q}) fixed-parameter forward y = x*W, float64, batch 2^{int(math.log2(batch))} "

@@ -764,12 +764,14 @@ cudaError_t launch_rep_ws(const RepDevice &rep, const double *X, const double *T
 // output signs, Walsh transform, flip by the input signs, scale by 1/S, which
 // is exact).
 //
-// Warps 0-3 (producers): thread 0 keeps kFwdAhead bulk loads of raw x tiles in
-// flight (completion on one mbarrier per stage). For tile k all producers
-// gather X' in place and arrive on full[stage]; then, once the consumers have
-// arrived on done[] for tile k - kFwdLag, they scatter its Y' back to raw rows
-// in place, and thread 0 stores the tile's rows with one bulk copy. A stage is
-// reloaded only after its store has finished reading it (bulk wait_group.read).
+// Warps 0-3 (producers): thread 0 keeps FwdPipe::AHEAD bulk loads of raw x
+// tiles (and, with RESID, target tiles) in flight (completion on one mbarrier
+// per stage). For tile k all producers gather X' in place and arrive on
+// full[stage]; then, once the consumers have arrived on done[] for tile
+// k - FwdPipe::LAG, they scatter its Y' back to raw rows in place (with RESID
+// they store r = y - t there, y computed exactly as without), and thread 0
+// stores the tile's rows with one bulk copy. A stage is reloaded only after its
+// store has finished reading it (bulk wait_group.read).
 // Warps 4-7 (consumers): GEMM 1 transposed with W'^T fragments resident, as in
 // rep_ws_kernel, from zero accumulators; Y' is written over the X' rows the
 // warp has just read.
@@ -789,20 +791,22 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
 
-template <int D, int S>
+template <int D, int S, bool RESID>
 __global__ void __launch_bounds__(kWsThreads, 2)
 rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ W,
-               const TermParameter terms, size_t batch, double *Y) {
+               const TermParameter terms, const double *__restrict__ T, size_t batch, double *Y) {
     using G = WsGeo<D, S>;
+    using P = FwdPipe<RESID>;
     constexpr int N = G::N, TS = G::TS, TILE = G::TILE;
+    constexpr int NST = P::STAGES, STAGE = P::ARRAYS * TILE;
     constexpr int kConsumers = kWsThreads - kWsProducers;
     constexpr int kBarScatter = 1;  // named barrier of the producer warps
     extern __shared__ __align__(16) double smem[];
     double *Wp = smem;                      // D * D
-    double *stages = Wp + D * D;            // kFwdStages x one x tile
-    uint64_t *loaded = reinterpret_cast<uint64_t *>(stages + kFwdStages * TILE);
-    uint64_t *full = loaded + kFwdStages;   // producers -> consumers: X' ready
-    uint64_t *done = full + kFwdStages;     // consumers -> producers: Y' ready
+    double *stages = Wp + D * D;            // NST x (x tile [, target tile])
+    uint64_t *loaded = reinterpret_cast<uint64_t *>(stages + NST * STAGE);
+    uint64_t *full = loaded + NST;          // producers -> consumers: X' ready
+    uint64_t *done = full + NST;            // consumers -> producers: Y' ready
     __shared__ unsigned s_gave_up;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -810,7 +814,7 @@ rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
     const int K = (size_t)blockIdx.x < tiles ? (int)((tiles - 1 - blockIdx.x) / gridDim.x + 1) : 0;
 
     if (tid == 0) {
-        for (int s = 0; s < kFwdStages; ++s) {
+        for (int s = 0; s < NST; ++s) {
             mbar_init(&loaded[s], 1);
             mbar_init(&full[s], kWsProducers);
             mbar_init(&done[s], kConsumers);
@@ -866,27 +870,28 @@ rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
         auto issue = [&](int k) {
             size_t first;
             const unsigned bytes = (unsigned)tile_rows(k, &first) * N * (unsigned)sizeof(double);
-            uint64_t *bar = &loaded[k % kFwdStages];
-            mbar_expect_tx(bar, bytes);
-            bulk_load(stages + (k % kFwdStages) * TILE, X + first * N, bytes, bar);
+            uint64_t *bar = &loaded[k % NST];
+            mbar_expect_tx(bar, P::ARRAYS * bytes);
+            bulk_load(stages + (k % NST) * STAGE, X + first * N, bytes, bar);
+            if (RESID) bulk_load(stages + (k % NST) * STAGE + TILE, T + first * N, bytes, bar);
         };
         if (tid == 0)
-            for (int k = 0; k < K && k < kFwdAhead; ++k) issue(k);
-        for (int k = 0; k < K + kFwdLag; ++k) {
+            for (int k = 0; k < K && k < P::AHEAD; ++k) issue(k);
+        for (int k = 0; k < K + P::LAG; ++k) {
             if (k < K) {
-                const int ahead = k + kFwdAhead;
+                const int ahead = k + P::AHEAD;
                 if (tid == 0 && ahead < K) {
-                    // The stage of `ahead` last held tile ahead - kFwdStages, whose store was
-                    // issued kFwdStorePending stores ago at the latest.
-                    if (ahead >= kFwdStages) bulk_wait_read<kFwdStorePending>();
+                    // The stage of `ahead` last held tile ahead - NST, whose store was
+                    // issued STORE_PENDING stores ago at the latest.
+                    if (ahead >= NST) bulk_wait_read<P::STORE_PENDING>();
                     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
                     issue(ahead);
                 }
-                const int st = k % kFwdStages;
-                if (!mbar_wait(&loaded[st], (unsigned)((k / kFwdStages) & 1))) atomicOr(&s_gave_up, 1u);
+                const int st = k % NST;
+                if (!mbar_wait(&loaded[st], (unsigned)((k / NST) & 1))) atomicOr(&s_gave_up, 1u);
                 size_t first;
                 const int valid = tile_rows(k, &first);
-                double *xs = stages + st * TILE;
+                double *xs = stages + st * STAGE;
                 double v[G::PER][S];
 #pragma unroll
                 for (int i = 0; i < G::PER; ++i) {
@@ -905,25 +910,32 @@ rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
                 }
                 mbar_arrive(&full[st]);
             }
-            const int j = k - kFwdLag;
+            const int j = k - P::LAG;
             if (j >= 0) {
-                const int st = j % kFwdStages;
-                if (!mbar_wait(&done[st], (unsigned)((j / kFwdStages) & 1))) atomicOr(&s_gave_up, 1u);
-                double *xs = stages + st * TILE;
-                double v[G::PER][S];
+                const int st = j % NST;
+                if (!mbar_wait(&done[st], (unsigned)((j / NST) & 1))) atomicOr(&s_gave_up, 1u);
+                double *xs = stages + st * STAGE;
+                double v[G::PER][S], tv[G::PER][S];
 #pragma unroll
                 for (int i = 0; i < G::PER; ++i)
 #pragma unroll
-                    for (int f = 0; f < S; ++f) v[i][f] = flip_sign(xs[G::SLOTS * i * N + woff[f]], out_sign[f]);
+                    for (int f = 0; f < S; ++f) {
+                        v[i][f] = flip_sign(xs[G::SLOTS * i * N + woff[f]], out_sign[f]);
+                        tv[i][f] = RESID ? xs[TILE + G::SLOTS * i * N + roff[f]] : 0.0;  // raw target blade
+                    }
                 named_sync(kBarScatter, kWsProducers);  // every Y' read is done before the in-place writes
                 const bool poison = *(volatile unsigned *)&s_gave_up != 0u;
 #pragma unroll
                 for (int i = 0; i < G::PER; ++i) {
                     walsh<S>(v[i]);
 #pragma unroll
-                    for (int t = 0; t < S; ++t)
+                    for (int t = 0; t < S; ++t) {
+                        // y exactly as the plain forward computes it (the scaling by 1/S is exact);
+                        // with RESID the stored value is r = y - t.
+                        const double y = flip_sign(v[i][t], in_sign[t]) * inv_s;
                         xs[G::SLOTS * i * N + roff[t]] =
-                            poison ? __longlong_as_double(0x7ff8000000000000ll) : flip_sign(v[i][t], in_sign[t]) * inv_s;
+                            poison ? __longlong_as_double(0x7ff8000000000000ll) : (RESID ? __dsub_rn(y, tv[i][t]) : y);
+                    }
                 }
                 asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic writes -> bulk store
                 named_sync(kBarScatter, kWsProducers);
@@ -938,8 +950,8 @@ rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
             asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
             // After a wait that gave up, bounded waits for loads that may still be in flight.
             if (*(volatile unsigned *)&s_gave_up != 0u)
-                for (int k = K > kFwdStages ? K - kFwdStages : 0; k < K; ++k)
-                    (void)mbar_wait(&loaded[k % kFwdStages], (unsigned)((k / kFwdStages) & 1));
+                for (int k = K > NST ? K - NST : 0; k < K; ++k)
+                    (void)mbar_wait(&loaded[k % NST], (unsigned)((k / NST) & 1));
         }
     } else {
         // ------------------------------------------------------------ consumers
@@ -953,9 +965,9 @@ rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
             else wa[i] = i < KT ? Wp[(4 * i + t4) * D + g] : 0.0;
         }
         for (int k = 0; k < K; ++k) {
-            const int st = k % kFwdStages;
-            if (!mbar_wait(&full[st], (unsigned)((k / kFwdStages) & 1))) atomicOr(&s_gave_up, 1u);
-            double *xs = stages + st * TILE;
+            const int st = k % NST;
+            if (!mbar_wait(&full[st], (unsigned)((k / NST) & 1))) atomicOr(&s_gave_up, 1u);
+            double *xs = stages + st * STAGE;
 #pragma unroll
             for (int j = 0; j < G::GPW; j += 2) {
                 int n0[2];
@@ -997,14 +1009,15 @@ rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
     }
 }
 
-template <int D, int S>
+template <int D, int S, bool RESID>
 cudaError_t launch_rep_fwd(const RepDevice &rep, const double *X, const double *W, const TermParameter &terms,
-                           double *Y, size_t batch, cudaStream_t stream) {
+                           const double *T, double *Y, size_t batch, cudaStream_t stream) {
     using G = WsGeo<D, S>;
+    using P = FwdPipe<RESID>;
     if (rep.raw_stride != G::N || rep.D != D || rep.S != S) return cudaErrorInvalidValue;
-    auto kernel = rep_fwd_kernel<D, S>;
-    const size_t smem =
-        (size_t)(D * D + kFwdStages * G::TILE) * sizeof(double) + 3 * kFwdStages * sizeof(uint64_t);
+    auto kernel = rep_fwd_kernel<D, S, RESID>;
+    const size_t smem = (size_t)(D * D + P::STAGES * P::ARRAYS * G::TILE) * sizeof(double) +
+                        3 * P::STAGES * sizeof(uint64_t);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     int per_sm = 1;
@@ -1015,17 +1028,19 @@ cudaError_t launch_rep_fwd(const RepDevice &rep, const double *X, const double *
     size_t grid = (size_t)device_sm_count() * (size_t)per_sm;
     if (grid > tiles) grid = tiles;
     if (grid < 1) grid = 1;
-    kernel<<<(unsigned)grid, kWsThreads, smem, stream>>>(rep, X, W, terms, batch, Y);
+    kernel<<<(unsigned)grid, kWsThreads, smem, stream>>>(rep, X, W, terms, T, batch, Y);
     return cudaGetLastError();
 }
 
+template <bool RESID>
 cudaError_t launch_rep_forward_impl(const RepDevice &rep, const double *X, const double *W,
-                                    const TermParameter &terms, double *Y, size_t batch, cudaStream_t stream) {
-    if (!rep_forward_supported(rep, X, Y)) return cudaErrorInvalidValue;
-    if (rep.D == 16 && rep.S == 4) return launch_rep_fwd<16, 4>(rep, X, W, terms, Y, batch, stream);
-    if (rep.D == 8 && rep.S == 8) return launch_rep_fwd<8, 8>(rep, X, W, terms, Y, batch, stream);
-    if (rep.D == 8 && rep.S == 4) return launch_rep_fwd<8, 4>(rep, X, W, terms, Y, batch, stream);
-    if (rep.D == 16 && rep.S == 2) return launch_rep_fwd<16, 2>(rep, X, W, terms, Y, batch, stream);
+                                    const TermParameter &terms, const double *T, double *Y, size_t batch,
+                                    cudaStream_t stream) {
+    if (!rep_forward_supported(rep, X, Y) || (RESID && ((uintptr_t)T & 15u) != 0u)) return cudaErrorInvalidValue;
+    if (rep.D == 16 && rep.S == 4) return launch_rep_fwd<16, 4, RESID>(rep, X, W, terms, T, Y, batch, stream);
+    if (rep.D == 8 && rep.S == 8) return launch_rep_fwd<8, 8, RESID>(rep, X, W, terms, T, Y, batch, stream);
+    if (rep.D == 8 && rep.S == 4) return launch_rep_fwd<8, 4, RESID>(rep, X, W, terms, T, Y, batch, stream);
+    if (rep.D == 16 && rep.S == 2) return launch_rep_fwd<16, 2, RESID>(rep, X, W, terms, T, Y, batch, stream);
     return cudaErrorInvalidValue;
 }
 
@@ -1041,13 +1056,26 @@ cudaError_t launch_rep_forward(const RepDevice &rep, const double *X, const doub
     TermParameter none;
     none.terms = 0;
     none.values = nullptr;
-    return launch_rep_forward_impl(rep, X, W, none, Y, batch, stream);
+    return launch_rep_forward_impl<false>(rep, X, W, none, nullptr, Y, batch, stream);
 }
 
 cudaError_t launch_rep_forward_terms(const RepDevice &rep, const double *X, const TermParameter &terms, double *Y,
                                      size_t batch, cudaStream_t stream) {
     if (terms.terms < 1 || terms.terms > 64) return cudaErrorInvalidValue;
-    return launch_rep_forward_impl(rep, X, nullptr, terms, Y, batch, stream);
+    return launch_rep_forward_impl<false>(rep, X, nullptr, terms, nullptr, Y, batch, stream);
+}
+
+bool rep_residual_supported(const RepDevice &rep, const double *X, const double *T, const double *R) {
+    return rep_forward_supported(rep, X, R) && ((uintptr_t)T & 15u) == 0u;
+}
+
+cudaError_t launch_rep_residual(const RepDevice &rep, const double *X, const double *W, const double *T, double *R,
+                                size_t batch, cudaStream_t stream) {
+    if (W == nullptr || T == nullptr) return cudaErrorInvalidValue;
+    TermParameter none;
+    none.terms = 0;
+    none.values = nullptr;
+    return launch_rep_forward_impl<true>(rep, X, W, none, T, R, batch, stream);
 }
 
 cudaError_t launch_rep_cycle(const RepDevice &rep, const double *X, const double *T, const double *W, size_t batch,

@@ -19,15 +19,20 @@ constexpr int kWsStages = 6;       // shared-memory stages per CTA
 
 // Forward kernel (rep_fwd_kernel): a stage holds one x tile (8 KB), which is
 // gathered in place, overwritten by Y', scattered back to raw y rows and
-// stored from the same stage.
-constexpr int kFwdStages = 12;  // shared-memory stages per CTA
-constexpr int kFwdAhead = 7;    // tiles whose bulk loads are in flight
-constexpr int kFwdLag = 2;      // the scatter of tile k - kFwdLag follows the gather of tile k
-// Bulk stores that may still be reading shared memory when a stage is
-// reloaded: the load of tile k + kFwdAhead reuses the stage of tile
-// k + kFwdAhead - kFwdStages, whose store was issued this many stores ago.
-constexpr int kFwdStorePending = kFwdStages - 1 - kFwdLag - kFwdAhead;
-static_assert(kFwdStorePending >= 0, "a stage is reloaded only after its store was issued");
+// stored from the same stage; with RESID the stage also holds the target tile
+// and the kernel stores r = y - t.
+template <bool RESID>
+struct FwdPipe {
+    static constexpr int ARRAYS = RESID ? 2 : 1;  // x tile (+ target tile) per stage
+    static constexpr int STAGES = RESID ? 6 : 12; // shared-memory stages per CTA
+    static constexpr int AHEAD = RESID ? 3 : 7;   // tiles whose bulk loads are in flight
+    static constexpr int LAG = 2;                 // the scatter of tile k - LAG follows the gather of tile k
+    // Bulk stores that may still be reading shared memory when a stage is
+    // reloaded: the load of tile k + AHEAD reuses the stage of tile
+    // k + AHEAD - STAGES, whose store was issued this many stores ago.
+    static constexpr int STORE_PENDING = STAGES - 1 - LAG - AHEAD;
+    static_assert(STORE_PENDING >= 0, "a stage is reloaded only after its store was issued");
+};
 
 template <int D, int S>
 struct WsGeo {

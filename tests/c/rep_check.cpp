@@ -96,36 +96,38 @@ static const char *check_ws_layout(const RepDevice &dev) {
     return nullptr;
 }
 
-// The forward kernel's pipeline (rep_fwd_kernel): producer iteration k issues
-// the load of tile k + kFwdAhead (after waiting until at most kFwdStorePending
-// bulk stores are pending), gathers tile k and scatters + stores tile
-// k - kFwdLag. Replays the order for many tile counts and checks that every
-// load goes into a stage whose previous tile was already stored, and that the
-// stores still pending at that moment are all later tiles.
+// The forward kernel's pipeline (rep_fwd_kernel, both FwdPipe variants):
+// producer iteration k issues the load of tile k + AHEAD (after waiting until
+// at most STORE_PENDING bulk stores are pending), gathers tile k and scatters
+// + stores tile k - LAG. Replays the order for many tile counts and checks that
+// every load goes into a stage whose previous tile was already stored, and
+// that the stores still pending at that moment are all later tiles.
+template <bool RESID>
 static const char *check_forward_pipeline() {
+    using P = FwdPipe<RESID>;
     for (int K = 1; K <= 64; ++K) {
         std::vector<int> stored;  // tiles in store-issue order
         std::vector<bool> issued(K, false);
-        for (int k = 0; k < K && k < kFwdAhead; ++k) issued[k] = true;  // prologue
-        for (int k = 0; k < K + kFwdLag; ++k) {
+        for (int k = 0; k < K && k < P::AHEAD; ++k) issued[k] = true;  // prologue
+        for (int k = 0; k < K + P::LAG; ++k) {
             if (k < K) {
-                const int ahead = k + kFwdAhead;
+                const int ahead = k + P::AHEAD;
                 if (ahead < K) {
-                    const int prev = ahead - kFwdStages;  // tile that last used the stage
+                    const int prev = ahead - P::STAGES;  // tile that last used the stage
                     if (prev >= 0) {
-                        // wait_group.read kFwdStorePending: all but the newest kFwdStorePending stores are done
+                        // wait_group.read STORE_PENDING: all but the newest STORE_PENDING stores are done
                         int pos = -1;
                         for (int i = 0; i < (int)stored.size(); ++i)
                             if (stored[i] == prev) pos = i;
                         if (pos < 0) return "stage reloaded before its store was issued";
-                        if ((int)stored.size() - pos <= kFwdStorePending)
+                        if ((int)stored.size() - pos <= P::STORE_PENDING)
                             return "stage reloaded while its store may still read it";
                     }
                     issued[ahead] = true;
                 }
                 if (!issued[k]) return "tile gathered before its load was issued";
             }
-            const int j = k - kFwdLag;
+            const int j = k - P::LAG;
             if (j >= 0 && j < K) stored.push_back(j);
         }
         if ((int)stored.size() != K) return "not every tile stored";
@@ -173,8 +175,12 @@ int main() {
     std::mt19937_64 rng(5);
     std::uniform_real_distribution<double> U(-1.0, 1.0);
     int cases = 0;
-    if (const char *why = check_forward_pipeline()) {
+    if (const char *why = check_forward_pipeline<false>()) {
         printf("FAIL forward pipeline: %s\n", why);
+        return 1;
+    }
+    if (const char *why = check_forward_pipeline<true>()) {
+        printf("FAIL residual pipeline: %s\n", why);
         return 1;
     }
     for (int n = 1; n <= 6; ++n) {

@@ -219,6 +219,17 @@ def test_unaligned_device_pointers(oracle):
         sync()
         assert tol_close(host(out)[1:].reshape(200, N), oracle.forward(sig, x, w, False)[1], TOL)
         assert tol_close(host(g), oracle.vjp(sig, x, t, True)[1], TOL)
+        # MSE-SGD step with 8-byte aligned residuals (the Cayley cycle kernel at every n)
+        res = dev(np.zeros(x.size + 1))
+        ro = ctypes.c_void_p(res.data_ptr() + 8)
+        dparam, dgrad, dloss = dev(w.copy()), dev(np.zeros(N)), dev(np.zeros(1))
+        assert L.geo_batch_gp_cuda_mse_sgd_step_f64(ctypes.byref(plan.dev), ptr(dev(x)), ptr(dev(t)), 200, 1e-3, 0,
+                                                    ptr(dparam), ro, ptr(dgrad), ptr(dloss), stream()) == 0
+        sync()
+        st, w_ref, mean_loss = oracle.sgd_step(sig, x, t, 1e-3, w, False)
+        assert st == 0
+        assert tol_close(host(res)[1:].reshape(200, N), oracle.forward(sig, x, w, False)[1] - t, TOL)
+        assert tol_close(host(dparam), w_ref, TOL) and tol_close(host(dloss)[0] / 200, mean_loss, TOL)
 
 
 @pytest.mark.parametrize("q", [0, 3])
