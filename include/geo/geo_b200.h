@@ -152,12 +152,13 @@ const double *geo_b200_trainer_device_parameter(const geo_b200_trainer_t *traine
  * (reference src/batch_gp_cuda.cu:252-286, src/batch_gp.c:107-161) without a
  * plan object. All arrays are device memory; asynchronous on `stream`;
  * reports argument and launch errors only, like the device ABI.
- *  CAYLEY: the kernel behind the device ABI's forward, bit-identical to it.
+ *  CAYLEY: the 2^n x 2^n sign-folded Cayley matrix on FP64 FMA units (any n).
  *  REPRESENTATION (n = 5, 6; inputs and outputs 16-byte aligned): X' = P x,
  *    Y' = X' W' on FP64 tensor cores, y = P^-1 Y'. Equal to the Cayley product
  *    up to rounding (within 1e-12 relative); INVALID_ARGUMENT where it is not
  *    available.
- *  AUTO: REPRESENTATION where available, else CAYLEY.
+ *  AUTO: REPRESENTATION where available, else CAYLEY; bit-identical to
+ *    geo_batch_gp_cuda_planned_forward_f64 on the same arrays (the same kernel).
  * device_parameter may be geo_b200_trainer_device_parameter(). Outputs may be
  * the inputs (in place) but must not overlap them otherwise. A non-finite
  * input coefficient makes every output coefficient of its sample non-finite
