@@ -520,6 +520,13 @@ def operator_legs(lib, X, world) -> dict:
     out["pairwise_f64_vjp"] = {"value": batch * world / (ms / 1e3), "unit": "products/s", "ms_per_launch": ms,
                                "bytes_per_product": 2560, "flops_per_product": 16384, "achieved_gbs": gbs,
                                "hbm_frac": gbs / hbm_peak, "fp64_tflops": tf, "fp64_frac": tf / FP64_DFMA_TFLOPS}
+    # Pairwise JVP: y_dot = a_dot b + a b_dot; 16384 flops, 2560 algorithmic bytes per product.
+    ms = _time_launches(lambda: lib.geo_b200_pairwise_gp_jvp_f64(6, sig, xp, bp, cp, zp, yp, batch, sp), world)
+    tf = batch * 16384 / (ms / 1e3) / 1e12
+    gbs = batch * 2560 / (ms / 1e3) / 1e9
+    out["pairwise_f64_jvp"] = {"value": batch * world / (ms / 1e3), "unit": "products/s", "ms_per_launch": ms,
+                               "bytes_per_product": 2560, "flops_per_product": 16384, "achieved_gbs": gbs,
+                               "hbm_frac": gbs / hbm_peak, "fp64_tflops": tf, "fp64_frac": tf / FP64_DFMA_TFLOPS}
     del Y, Bm, Cb, Z
     torch.cuda.empty_cache()
     out["workload"] = ("Cl(6,0) per-element operators, float64, 2^%d elements per GPU (operands resident, "

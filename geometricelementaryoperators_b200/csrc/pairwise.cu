@@ -487,7 +487,15 @@ constexpr int kF64Box = kF64Rows * 16;         // doubles of one [32][16] box (4
 constexpr int kF64Stages = 2;
 constexpr int kF64StageBoxes = 8;              // a: 4 boxes, b: 4 boxes
 // + 1024 bytes to align the boxes to the 1024-byte period of the 128-byte swizzle
-constexpr size_t kF64Smem = ((size_t)kF64Stages * kF64StageBoxes + kF64Compute) * kF64Box * sizeof(double) + 1024;
+// Output area of a compute warp: the swizzled [32][16] box of the TMA store, or
+// (accumulating launches) 32 per-lane slots of 16 doubles at an 18-double
+// stride (16-byte aligned, conflict-free 16-byte writes); 5 KB keeps every box
+// on the 1024-byte period of the swizzle.
+constexpr int kF64OutArea = 640;                  // doubles per compute warp (5 KB)
+constexpr int kF64SlotStride = 18;                // doubles between the lanes' slots
+static_assert(kF64Rows * kF64SlotStride <= kF64OutArea && kF64Box <= kF64OutArea, "output area");
+constexpr size_t kF64Smem =
+    ((size_t)kF64Stages * kF64StageBoxes * kF64Box + (size_t)kF64Compute * kF64OutArea) * sizeof(double) + 1024;
 
 struct F64BlockSigns {
     uint16_t alpha[4][4];  // [L0][O0] bit i: a_{16 L0 + i} enters block (L0, O0) negated
@@ -547,12 +555,16 @@ __device__ __forceinline__ void f64_wait(uint64_t *bar, unsigned parity) {
 template <int NEG>
 __global__ void __launch_bounds__(kF64Threads, 2)
 pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                           const __grid_constant__ CUtensorMap map_out, const F64BlockSigns signs, size_t batch) {
+                           const __grid_constant__ CUtensorMap map_out, const F64BlockSigns signs, size_t batch,
+                           double *acc_out) {
+    // acc_out == null: outputs are stored (TMA tensor store of a swizzled box).
+    // acc_out != null: outputs are added into acc_out[batch][64] by a bulk
+    // reduce-add per row (one rounding per element), for the JVP's second product.
     extern __shared__ unsigned char f64_raw[];
     __shared__ __align__(8) uint64_t full[kF64Stages], empty[kF64Stages];
     __shared__ F64BlockSigns sgn;
     double *base = reinterpret_cast<double *>(((uintptr_t)f64_raw + 1023) & ~(uintptr_t)1023);
-    double *outbox = base + kF64Stages * kF64StageBoxes * kF64Box;  // one box per compute warp
+    double *outbox = base + kF64Stages * kF64StageBoxes * kF64Box;  // one output area per compute warp
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const size_t tiles = (batch + kF64Rows - 1) / kF64Rows;
     const int K = (size_t)blockIdx.x < tiles ? (int)((tiles - 1 - blockIdx.x) / gridDim.x + 1) : 0;
@@ -588,7 +600,7 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
         return;
     }
     // ---- compute warps
-    double *ob = outbox + warp * kF64Box;
+    double *ob = outbox + warp * kF64OutArea;
     for (int k = 0; k < K; ++k) {
         const int s = k % kF64Stages;
         f64_wait(&full[s], (unsigned)((k / kF64Stages) & 1));
@@ -629,21 +641,44 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(&empty[s])) : "memory");
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) acc[kk] = flip_bit(acc[kk], (prev >> kk) & 1u);
-        // The store of tile k - 1 from this warp's box must have finished reading it.
-        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
-        __syncwarp();
+        const size_t row0 = (blockIdx.x + (size_t)k * gridDim.x) * kF64Rows;
+        if (acc_out == nullptr) {
+            // The store of tile k - 1 from this warp's box must have finished reading it.
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+            __syncwarp();
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<double2 *>(&ob[sw128d(lane, j)]) = make_double2(acc[2 * j], acc[2 * j + 1]);
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-        __syncwarp();
-        if (lane == 0) {
-            const int row = (int)((blockIdx.x + (size_t)k * gridDim.x) * kF64Rows);
-            tma_store_2d(&map_out, 16 * warp, row, ob);
-            asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+            for (int j = 0; j < 8; ++j)
+                *reinterpret_cast<double2 *>(&ob[sw128d(lane, j)]) = make_double2(acc[2 * j], acc[2 * j + 1]);
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&map_out, 16 * warp, (int)row0, ob);
+                asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+            }
+        } else {
+            // Each lane adds its 16 outputs into its own row: its slot's previous
+            // reduce (tile k - 1, issued by this lane) must have read the slot.
+            asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+            double *slot = ob + lane * kF64SlotStride;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                *reinterpret_cast<double2 *>(&slot[2 * j]) = make_double2(acc[2 * j], acc[2 * j + 1]);
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+            const size_t row = row0 + (size_t)lane;
+            if (row < batch) {
+                asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f64 [%0], [%1], 128;\n" ::"l"(
+                                 acc_out + row * 64 + 16 * warp),
+                             "r"(smem_u32(slot))
+                             : "memory");
+                asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+            }
         }
     }
-    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+    if (acc_out == nullptr) {
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+    } else {
+        asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+    }
 }
 
 // [rows][64] float64 tensor, [32][16] boxes, 128-byte swizzle, zero fill.
@@ -694,7 +729,7 @@ bool f64_block_signs(const geo::SignPlan &plan, int neg_low, bool rev_a, bool re
 
 template <int NEG>
 cudaError_t launch_f64_tma_neg(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mo,
-                               const F64BlockSigns &signs, size_t batch, cudaStream_t stream) {
+                               const F64BlockSigns &signs, size_t batch, double *acc_out, cudaStream_t stream) {
     auto kernel = pairwise_f64_n6_tma_kernel<NEG>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kF64Smem);
     if (e != cudaSuccess) return e;
@@ -705,16 +740,16 @@ cudaError_t launch_f64_tma_neg(const CUtensorMap &ma, const CUtensorMap &mb, con
     const size_t tiles = (batch + kF64Rows - 1) / kF64Rows;
     size_t grid = (size_t)geo::device_sm_count() * (size_t)per_sm;
     if (grid > tiles) grid = tiles;
-    kernel<<<(unsigned)grid, kF64Threads, kF64Smem, stream>>>(ma, mb, mo, signs, batch);
+    kernel<<<(unsigned)grid, kF64Threads, kF64Smem, stream>>>(ma, mb, mo, signs, batch, acc_out);
     return cudaGetLastError();
 }
 
 template <int... NEG>
 cudaError_t launch_f64_tma_dispatch(int neg, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mo,
-                                    const F64BlockSigns &signs, size_t batch, cudaStream_t stream,
+                                    const F64BlockSigns &signs, size_t batch, double *acc_out, cudaStream_t stream,
                                     std::integer_sequence<int, NEG...>) {
     cudaError_t e = cudaErrorInvalidValue;
-    ((neg == NEG ? (e = launch_f64_tma_neg<NEG>(ma, mb, mo, signs, batch, stream), true) : false) || ...);
+    ((neg == NEG ? (e = launch_f64_tma_neg<NEG>(ma, mb, mo, signs, batch, acc_out, stream), true) : false) || ...);
     return e;
 }
 
@@ -722,7 +757,7 @@ cudaError_t launch_f64_tma_dispatch(int neg, const CUtensorMap &ma, const CUtens
 // (unaligned operands, no tensor-map encoder, sign table that does not factor).
 bool launch_pairwise_f64_fast(const geo::SignPlan &plan, const int8_t *signature, const double *left,
                               const double *right, double *out, size_t batch, cudaStream_t stream, cudaError_t *err,
-                              bool rev_left = false, bool rev_right = false) {
+                              bool rev_left = false, bool rev_right = false, bool accumulate = false) {
     if (plan.blades != 64 || ((uintptr_t)left | (uintptr_t)right | (uintptr_t)out) & 15u) return false;
     int neg_low = 0;
     for (int a = 0; a < 4; ++a)
@@ -732,7 +767,8 @@ bool launch_pairwise_f64_fast(const geo::SignPlan &plan, const int8_t *signature
     CUtensorMap ma, mb, mo;
     if (!encode_rows_f64(&ma, left, batch) || !encode_rows_f64(&mb, right, batch) || !encode_rows_f64(&mo, out, batch))
         return false;
-    *err = launch_f64_tma_dispatch(neg_low, ma, mb, mo, signs, batch, stream, std::make_integer_sequence<int, 16>{});
+    *err = launch_f64_tma_dispatch(neg_low, ma, mb, mo, signs, batch, accumulate ? out : nullptr, stream,
+                                   std::make_integer_sequence<int, 16>{});
     return true;
 }
 
@@ -810,6 +846,23 @@ extern "C" geo_b200_status_t geo_b200_pairwise_gp_jvp_f64(uint8_t dimension, con
                                                           cudaStream_t stream) {
     if (device_left_tangent == nullptr || device_right_tangent == nullptr || device_out_tangent == nullptr)
         return GEO_B200_INVALID_ARGUMENT;
+    // n = 6: two forward products on the TMA kernel, out = a_dot b, then
+    // out += a b_dot (bulk reduce-add, one rounding per element).
+    const geo::SignPlan *plan = dimension == 6 ? geo::cached_sign_plan(6, signature, 0) : nullptr;
+    const bool al = ((uintptr_t)device_left | (uintptr_t)device_right | (uintptr_t)device_left_tangent |
+                     (uintptr_t)device_right_tangent | (uintptr_t)device_out_tangent) % 16u == 0u;
+    if (plan != nullptr && al && device_left != nullptr && device_right != nullptr && batch > 0 &&
+        tensor_map_encoder() != nullptr) {
+        cudaError_t e = cudaSuccess;
+        if (launch_pairwise_f64_fast(*plan, signature, device_left_tangent, device_right, device_out_tangent, batch,
+                                     stream, &e)) {
+            if (e == cudaSuccess &&
+                !launch_pairwise_f64_fast(*plan, signature, device_left, device_right_tangent, device_out_tangent,
+                                          batch, stream, &e, false, false, true))
+                e = cudaErrorInvalidValue;  // cannot happen: same plan, alignment and sizes as the first launch
+            return from_cuda(e);
+        }
+    }
     return launch_pairwise<double, kPairJvp>(dimension, signature, device_left, 0, device_right, device_left_tangent,
                                              device_right_tangent, device_out_tangent, nullptr, batch, stream);
 }
