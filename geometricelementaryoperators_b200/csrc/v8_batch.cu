@@ -73,36 +73,30 @@ __device__ __forceinline__ double signed_by(double v, uint64_t word, int bit) {
     return __hiloint2double(__double2hiint(v) ^ flip, __double2loint(v));
 }
 
-// A multivector held by a warp as (lo, hi): lane l has blades l and l + 32.
-// Blade q, on every lane:
-__device__ __forceinline__ double blade_at(double lo, double hi, int q) {
-    return __shfl_sync(0xffffffffu, q < 32 ? lo : hi, q & 31);
-}
-// Blade lane ^ q (first blade of the lane) and (lane + 32) ^ q (second):
-__device__ __forceinline__ double xor_first(double lo, double hi, int q) {
-    return __shfl_xor_sync(0xffffffffu, q < 32 ? lo : hi, q & 31);
-}
-__device__ __forceinline__ double xor_second(double lo, double hi, int q) {
-    return __shfl_xor_sync(0xffffffffu, q < 32 ? hi : lo, q & 31);
-}
-// Sequential sums over the blades in blade order (the reference's loops), on
-// every lane; operands come from registers, so only the adds form a chain.
-__device__ __forceinline__ double blade_dot(double x0, double x1, double y0, double y1, int N) {
+// Sequential sums over the blades in blade order (the reference's loops),
+// computed identically on every lane from the node values in the warp's
+// scratch: each load reads one address for the whole warp (a broadcast), two
+// blades at a time, so only the chain of adds is serial.
+template <int N>
+__device__ __forceinline__ double blade_dot(const double *x, const double *y) {
     double acc = 0.0;
 #pragma unroll 8
-    for (int q = 0; q < 64; ++q) {
-        if (q >= N) break;
-        acc = add(acc, mul(blade_at(x0, x1, q), blade_at(y0, y1, q)));
+    for (int q = 0; q < N; q += 2) {
+        const double2 u = *reinterpret_cast<const double2 *>(x + q);
+        const double2 v = *reinterpret_cast<const double2 *>(y + q);
+        acc = add(acc, mul(u.x, v.x));
+        acc = add(acc, mul(u.y, v.y));
     }
     return acc;
 }
-__device__ __forceinline__ double half_squared_norm(double x0, double x1, int N) {
+template <int N>
+__device__ __forceinline__ double half_squared_norm(const double *x) {
     double acc = 0.0;
 #pragma unroll 8
-    for (int q = 0; q < 64; ++q) {
-        if (q >= N) break;
-        const double v = blade_at(x0, x1, q);
-        acc = add(acc, mul(mul(0.5, v), v));
+    for (int q = 0; q < N; q += 2) {
+        const double2 u = *reinterpret_cast<const double2 *>(x + q);
+        acc = add(acc, mul(mul(0.5, u.x), u.x));
+        acc = add(acc, mul(mul(0.5, u.y), u.y));
     }
     return acc;
 }
@@ -174,18 +168,16 @@ __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(c
                 case GEO_V8_NODE_ADD: o0 = add(L[b0], R[b0]); o1 = add(L[b1], R[b1]); break;
                 case GEO_V8_NODE_SCALE: o0 = mul(L[b0], nd.scalar); o1 = mul(L[b1], nd.scalar); break;
                 case GEO_V8_NODE_GEOMETRIC_PRODUCT: {
-                    // reference src/operator_kernel.c:412-447: left-blade-major, zero left coefficients skipped
-                    const double L0 = L[b0], L1 = L[b1], R0 = R[b0], R1 = R[b1];
+                    // reference src/operator_kernel.c:412-447: left-blade-major, zero left coefficients skipped;
+                    // left blade l by a broadcast load, right blade l ^ b by a per-lane load (both in L1)
                     double c0 = 0.0, c1 = 0.0;
 #pragma unroll 8
-                    for (int l = 0; l < 64; ++l) {
-                        if (l >= N) break;
-                        const double lv = blade_at(L0, L1, l);
-                        const double r0 = xor_first(R0, R1, l), r1 = xor_second(R0, R1, l);
+                    for (int l = 0; l < N; ++l) {
+                        const double lv = L[l];
                         if (lv == 0.0) continue;
                         const uint64_t negl = a.neg[l];
-                        if (l0) c0 = add(c0, signed_by(mul(lv, r0), negl, l ^ b0));
-                        if (l1) c1 = add(c1, signed_by(mul(lv, r1), negl, l ^ b1));
+                        if (l0) c0 = add(c0, signed_by(mul(lv, R[l ^ b0]), negl, l ^ b0));
+                        if (l1) c1 = add(c1, signed_by(mul(lv, R[l ^ b1]), negl, l ^ b1));
                     }
                     o0 = c0;
                     o1 = c1;
@@ -213,7 +205,7 @@ __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(c
                     break;
                 }
                 case GEO_V8_NODE_EUCLIDEAN_NORMALIZE: {
-                    const double n2 = blade_dot(L[b0], L[b1], L[b0], L[b1], N);
+                    const double n2 = blade_dot<N>(L, L);
                     const double floor_value = nd.scalar > 0.0 ? nd.scalar : 1e-12;
                     if (!isfinite(n2) || n2 <= mul(floor_value, floor_value)) { fail = GEO_V8_NUMERIC_FAILURE; fnode = i; break; }
                     const double inverse = __ddiv_rn(1.0, __dsqrt_rn(n2));
@@ -222,7 +214,7 @@ __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(c
                     break;
                 }
                 case GEO_V8_NODE_SQUARED_NORM: {
-                    const double sum = half_squared_norm(L[b0], L[b1], N);
+                    const double sum = half_squared_norm<N>(L);
                     o0 = lane == 0 ? sum : 0.0;
                     o1 = 0.0;
                     break;
@@ -281,22 +273,21 @@ __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(c
                     if (ln->requires_grad) ok = accumulate2(a, lc, c0, c1, nd.scalar, b0, b1);
                     break;
                 case GEO_V8_NODE_GEOMETRIC_PRODUCT: {
-                    // reference src/operator_kernel.c:494-539
-                    const double C0 = cot[b0], C1 = cot[b1];
-                    const double Lv0 = lvv[b0], Lv1 = lvv[b1], Rv0 = rvv[b0], Rv1 = rvv[b1];
-                    const uint64_t neg0 = a.neg[b0], neg1 = a.neg[b1];
+                    // reference src/operator_kernel.c:494-539; blade q of the operands by broadcast
+                    // loads, cotangent blade b ^ q by a per-lane load (all in L1)
+                    const uint64_t neg0 = a.neg[b0 & 63], neg1 = a.neg[b1 & 63];
                     double la0 = 0.0, la1 = 0.0, ra0 = 0.0, ra1 = 0.0;
 #pragma unroll 8
-                    for (int q = 0; q < 64; ++q) {
-                        if (q >= N) break;
-                        const double cq0 = xor_first(C0, C1, q), cq1 = xor_second(C0, C1, q);  // cot[b ^ q]
-                        const double rq = blade_at(Rv0, Rv1, q), lq = blade_at(Lv0, Lv1, q);
+                    for (int q = 0; q < N; ++q) {
+                        const double rq = rvv[q], lq = lvv[q];
                         const uint64_t negq = a.neg[q];
                         if (l0) {
+                            const double cq0 = cot[b0 ^ q];
                             la0 = add(la0, mul(signed_by(cq0, neg0, q), rq));
                             ra0 = add(ra0, mul(signed_by(cq0, negq, b0), lq));
                         }
                         if (l1) {
+                            const double cq1 = cot[b1 ^ q];
                             la1 = add(la1, mul(signed_by(cq1, neg1, q), rq));
                             ra1 = add(ra1, mul(signed_by(cq1, negq, b1), lq));
                         }
@@ -361,8 +352,8 @@ __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(c
                     break;
                 case GEO_V8_NODE_EUCLIDEAN_NORMALIZE: {
                     const double *ov = vals + (size_t)cursor * 64;
-                    const double n2 = blade_dot(lvv[b0], lvv[b1], lvv[b0], lvv[b1], N);
-                    const double dot = blade_dot(ov[b0], ov[b1], cot[b0], cot[b1], N);
+                    const double n2 = blade_dot<N>(lvv, lvv);
+                    const double dot = blade_dot<N>(ov, cot);
                     if (!isfinite(n2) || n2 <= 0.0 || !isfinite(dot)) { ok = false; break; }
                     if (ln->requires_grad) {
                         const double inverse = __ddiv_rn(1.0, __dsqrt_rn(n2));
