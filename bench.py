@@ -536,6 +536,38 @@ def operator_legs(lib, X, world) -> dict:
     return out
 
 
+def cl41_leg(lib, X, T, world, steps) -> dict:
+    """Cl(4,1) (n = 5, 32 blades, mixed signature) full-cycle Adam steps with the
+    parameter on either side, on the resident headline arrays read as 2^23 rows of
+    32 blades (x and t 2 GiB each, 512 B per sample)."""
+    import torch
+
+    from geometricelementaryoperators_b200 import abi
+
+    batch = X.numel() // 32
+    sig = abi.sig_array([1, 1, 1, 1, -1])
+    sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    xp, tp = ctypes.c_void_p(X.data_ptr()), ctypes.c_void_p(T.data_ptr())
+    w0 = np.ascontiguousarray(np.random.default_rng(41).normal(0.0, 0.125, 32))
+    cfg = abi.OptimizerConfig(2, 1e-3, 0.9, 0.999, 1e-8)
+    hbm_peak, _ = peaks()
+    out = {"workload": f"Cl(4,1) full-cycle training step (forward + parameter VJP + MSE + Adam), float64, batch "
+                       f"2^{int(math.log2(batch))} per GPU, 512 B per sample"}
+    for side, name in ((0, "right"), (1, "left")):
+        h = ctypes.c_void_p()
+        assert lib.geo_b200_trainer_create(ctypes.byref(h), 5, sig, side, w0.ctypes.data_as(ctypes.c_void_p),
+                                           ctypes.byref(cfg)) == 0
+        ms = _time_launches(lambda: lib.geo_b200_trainer_step_device(h, xp, tp, batch, 1.0 / batch, sp), world,
+                            reps=steps)
+        assert lib.geo_b200_trainer_sync(h, None) == 0
+        algo = lib.geo_b200_trainer_algorithm(h)
+        lib.geo_b200_trainer_destroy(h)
+        gbs = batch * 512 / (ms / 1e3) / 1e9
+        out[name] = {"value": batch * world / (ms / 1e3), "unit": "training samples/s", "ms_per_step": ms,
+                     "achieved_gbs": gbs, "hbm_frac": gbs / hbm_peak, "algorithm": ALGORITHM_NAMES.get(algo, algo)}
+    return out
+
+
 def forward_leg(lib, X, q, world) -> dict:
     """Fixed-parameter forward y = x*W, Cl(6-q,q), float64, on the batch already
     resident for the training step (2 GiB of x read, 2 GiB of y written per
@@ -712,6 +744,7 @@ def run_b200(args, world, rank, local):
         # Fixed-parameter forward (multivector products/s) on the same resident batch.
         extras["forward"] = forward_leg(lib, X, q, world)
         extras["operators"] = operator_legs(lib, X, world)
+        extras["cl41"] = cl41_leg(lib, X, T, world, args.steps)
         # Same step on Cl(3,3) (the second signature of the headline config).
         X2, T2, w2 = X, T, w0
         tr33 = Trainer(lib, [1, 1, 1, -1, -1, -1], w2)
@@ -790,6 +823,8 @@ def run_b200(args, world, rank, local):
             line["forward"] = extras["forward"]
         if "operators" in extras:
             line["operators"] = extras["operators"]
+        if "cl41" in extras:
+            line["cl41"] = extras["cl41"]
         if world == 1 and not args.no_extras:
             line["cpu_baseline"] = cpu_baseline_leg(q)
             line["v8_graph"]["cpu_baseline"] = v8_graph_reference_leg()

@@ -55,6 +55,7 @@ geo_batch_gp_cuda_status_t launch_status(cudaError_t e) {
 geo_batch_gp_cuda_status_t forward(const geo_batch_gp_cuda_plan_t *plan, const double *device_inputs,
                                    size_t batch_size, const double *device_parameter, int parameter_on_left,
                                    double *device_outputs, cudaStream_t stream) {
+    geo::NvtxRange range("geo_batch_gp_cuda.forward");
     if (!plan_usable(plan) || device_inputs == nullptr || device_parameter == nullptr ||
         device_outputs == nullptr || batch_size == 0) {
         return GEO_BATCH_GP_CUDA_INVALID_ARGUMENT;
@@ -74,6 +75,7 @@ geo_batch_gp_cuda_status_t forward(const geo_batch_gp_cuda_plan_t *plan, const d
 geo_batch_gp_cuda_status_t vjp(const geo_batch_gp_cuda_plan_t *plan, const double *device_inputs,
                                const double *device_output_cotangents, size_t batch_size, int parameter_on_left,
                                double *device_parameter_cotangent, cudaStream_t stream) {
+    geo::NvtxRange range("geo_batch_gp_cuda.parameter_vjp");
     if (!plan_usable(plan) || device_inputs == nullptr || device_output_cotangents == nullptr ||
         device_parameter_cotangent == nullptr || batch_size == 0) {
         return GEO_BATCH_GP_CUDA_INVALID_ARGUMENT;
@@ -110,6 +112,7 @@ geo_batch_gp_cuda_status_t sgd_step(const geo_batch_gp_cuda_plan_t *plan, const 
                                     const double *device_targets, size_t batch_size, double learning_rate,
                                     int parameter_on_left, double *device_parameter, double *device_residuals,
                                     double *device_gradient, double *device_loss, cudaStream_t stream) {
+    geo::NvtxRange range("geo_batch_gp_cuda.mse_sgd_step");
     if (!plan_usable(plan) || device_inputs == nullptr || device_targets == nullptr || device_parameter == nullptr ||
         device_residuals == nullptr || device_gradient == nullptr || device_loss == nullptr || batch_size == 0 ||
         !isfinite(learning_rate) || learning_rate <= 0.0) {

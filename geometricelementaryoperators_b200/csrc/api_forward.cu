@@ -11,6 +11,7 @@ extern "C" geo_b200_status_t geo_b200_forward_f64(uint8_t dimension, const int8_
                                                   geo_b200_algorithm_t algorithm, const double *device_inputs,
                                                   const double *device_parameter, double *device_outputs,
                                                   size_t batch_size, cudaStream_t stream) {
+    geo::NvtxRange range("geo_b200.forward");
     if (!geo::dimension_valid(dimension)) return GEO_B200_UNSUPPORTED_DIMENSION;
     if (signature == nullptr || !geo::signature_valid(signature, dimension) || device_inputs == nullptr ||
         device_parameter == nullptr || device_outputs == nullptr || batch_size == 0)

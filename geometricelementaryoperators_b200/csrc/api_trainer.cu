@@ -246,6 +246,7 @@ extern "C" void geo_b200_trainer_destroy(geo_b200_trainer_t *t) {
 extern "C" geo_b200_status_t geo_b200_trainer_accumulate_device(geo_b200_trainer_t *t, const double *device_inputs,
                                                                 const double *device_targets, size_t batch,
                                                                 cudaStream_t stream) {
+    geo::NvtxRange range("geo_b200.trainer.accumulate");
     if (t == nullptr || device_inputs == nullptr || device_targets == nullptr || batch == 0)
         return GEO_B200_INVALID_ARGUMENT;
     int ctas = 0;
@@ -263,6 +264,7 @@ extern "C" geo_b200_status_t geo_b200_trainer_accumulate_device(geo_b200_trainer
 
 extern "C" geo_b200_status_t geo_b200_trainer_apply(geo_b200_trainer_t *t, double gradient_scale,
                                                     cudaStream_t stream) {
+    geo::NvtxRange range("geo_b200.trainer.apply");
     if (t == nullptr || !isfinite(gradient_scale) || gradient_scale <= 0.0) return GEO_B200_INVALID_ARGUMENT;
     geo::OptimizerArgs opt{};
     opt.kind = t->config.optimizer == GEO_B200_OPTIMIZER_ADAM ? geo::kOptAdamV8 : geo::kOptSgdV8;
@@ -315,6 +317,7 @@ extern "C" geo_b200_status_t geo_b200_trainer_step_device(geo_b200_trainer_t *t,
 }
 
 extern "C" geo_b200_status_t geo_b200_trainer_sync(geo_b200_trainer_t *t, double *loss_sum) {
+    geo::NvtxRange range("geo_b200.trainer.sync");
     if (t == nullptr) return GEO_B200_INVALID_ARGUMENT;
     if (t->last_stream != nullptr || t->comm != nullptr) {
         const geo_b200_status_t w = wait_stream(t->last_stream, t->comm);
@@ -338,6 +341,7 @@ extern "C" geo_b200_status_t geo_b200_trainer_sync(geo_b200_trainer_t *t, double
 extern "C" geo_b200_status_t geo_b200_trainer_step_host(geo_b200_trainer_t *t, const double *inputs,
                                                         const double *targets, size_t batch, double gradient_scale,
                                                         double *loss_sum) {
+    geo::NvtxRange range("geo_b200.trainer.step_host");
     if (t == nullptr || inputs == nullptr || targets == nullptr || batch == 0) return GEO_B200_INVALID_ARGUMENT;
     const size_t values = batch * (size_t)t->blades;
     const bool x_dev = geo::classify_pointer(inputs) == geo::Residency::kDevice;

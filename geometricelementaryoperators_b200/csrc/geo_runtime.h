@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -33,5 +34,14 @@ Residency classify_pointer(const void *ptr);
 
 // Copy helper that accepts any residency on either side (synchronous on `stream`).
 cudaError_t copy_any(void *dst, const void *src, size_t bytes, cudaStream_t stream);
+
+// Named host range for profilers (NVTX, header-only: a no-op unless a tool is
+// attached): marks the enqueue of an entry point's launches.
+struct NvtxRange {
+    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange &) = delete;
+    NvtxRange &operator=(const NvtxRange &) = delete;
+};
 
 }  // namespace geo
