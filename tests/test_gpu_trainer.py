@@ -245,3 +245,36 @@ def test_representation_matches_cayley_full_size(q):
     assert tol_close(l1, l2, TOL)
     for a, b in zip(s1[:3], s2[:3]):
         assert tol_close(a, b, TOL), max_violation(a, b, TOL)
+
+
+def test_large_batch_step_is_additive():
+    """2^25 + 7 Cl(6,0) samples (32 GiB resident, eight times the headline
+    batch; tile and record indexing far past 2^31 bytes): one whole-batch SGD
+    step equals two half-batch accumulations followed by one update, and the
+    reported loss sums agree (1e-12)."""
+    import torch
+
+    L = abi.lib()
+    sig = canonical_signature(6, 0)
+    B = (1 << 25) + 7
+    gen = torch.Generator(device="cuda").manual_seed(77)
+    X = torch.rand((B, 64), dtype=torch.float64, device="cuda", generator=gen).mul_(2).sub_(1)
+    T = torch.rand((B, 64), dtype=torch.float64, device="cuda", generator=gen).mul_(2).sub_(1)
+    w0 = normal(78, (64,), 0.125)
+    whole = Trainer(sig, False, w0, 1, 1e-2)
+    assert whole.step(X, T, B, 1.0 / B) == 0
+    st, loss_whole = whole.sync()
+    assert st == 0
+    split = Trainer(sig, False, w0, 1, 1e-2)
+    half = B // 2 + 13
+    for xs, ts, b in ((X[:half], T[:half], half), (X[half:], T[half:], B - half)):
+        assert L.geo_b200_trainer_accumulate_device(split.h, ptr(xs), ptr(ts), b, stream()) == 0
+    assert L.geo_b200_trainer_apply(split.h, 1.0 / B, stream()) == 0
+    st, loss_split = split.sync()
+    assert st == 0
+    assert tol_close(loss_whole, loss_split, TOL)
+    w1, _, _, n1 = whole.state()
+    w2, _, _, n2 = split.state()
+    assert n1 == n2 == 1
+    assert tol_close(w1, w2, TOL), max_violation(w1, w2, TOL)
+    assert not np.array_equal(w1, w0)
