@@ -792,7 +792,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 }
 
 template <int D, int S, bool RESID>
-__global__ void __launch_bounds__(kWsThreads, 2)
+__global__ void __launch_bounds__(kWsThreads, FwdPipe<RESID>::CTAS_PER_SM)
 rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ W,
                const TermParameter terms, const double *__restrict__ T, size_t batch, double *Y) {
     using G = WsGeo<D, S>;

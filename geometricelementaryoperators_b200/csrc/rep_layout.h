@@ -24,8 +24,11 @@ constexpr int kWsStages = 6;       // shared-memory stages per CTA
 template <bool RESID>
 struct FwdPipe {
     static constexpr int ARRAYS = RESID ? 2 : 1;  // x tile (+ target tile) per stage
-    static constexpr int STAGES = RESID ? 6 : 12; // shared-memory stages per CTA
-    static constexpr int AHEAD = RESID ? 3 : 7;   // tiles whose bulk loads are in flight
+    static constexpr int STAGES = RESID ? 6 : 8;  // shared-memory stages per CTA
+    static constexpr int AHEAD = RESID ? 3 : 4;   // tiles whose bulk loads are in flight
+    // CTAs per SM (the plain forward's 66 KB ring fits three; measured faster
+    // than 12 stages at two CTAs per SM)
+    static constexpr int CTAS_PER_SM = RESID ? 2 : 3;
     static constexpr int LAG = 2;                 // the scatter of tile k - LAG follows the gather of tile k
     // Bulk stores that may still be reading shared memory when a stage is
     // reloaded: the load of tile k + AHEAD reuses the stage of tile
