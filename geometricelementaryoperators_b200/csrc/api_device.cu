@@ -103,11 +103,11 @@ geo_batch_gp_cuda_status_t vjp(const geo_batch_gp_cuda_plan_t *plan, const doubl
 
 // Forward -> residual (stored) -> loss sum -> VJP -> SGD, as the reference's
 // five-launch sequence (src/batch_gp_cuda.cu:152-196). n = 5, 6 with 16-byte
-// aligned operands: r = y - t by the representation forward (y exactly as the
+// aligned operands: one representation pass stores r = y - t (y exactly as the
 // forward above computes it, so targets equal to its outputs give zero
-// residuals, loss and gradient, as in the reference), then the representation
-// parameter VJP of r (which also sums 0.5 |r|^2) and the update; otherwise the
-// fused Cayley cycle kernel and the update.
+// residuals, loss and gradient, as in the reference) and reduces the parameter
+// VJP of r with 0.5 |r|^2, then the update; otherwise the fused Cayley cycle
+// kernel and the update.
 geo_batch_gp_cuda_status_t sgd_step(const geo_batch_gp_cuda_plan_t *plan, const double *device_inputs,
                                     const double *device_targets, size_t batch_size, double learning_rate,
                                     int parameter_on_left, double *device_parameter, double *device_residuals,
@@ -124,12 +124,9 @@ geo_batch_gp_cuda_status_t sgd_step(const geo_batch_gp_cuda_plan_t *plan, const 
     int ctas = 0;
     const geo::RepDevice *rep = geo::cached_rep_device(plan->dimension, plan->signature, parameter_on_left != 0);
     cudaError_t e;
-    if (rep != nullptr && geo::rep_residual_supported(*rep, device_inputs, device_targets, device_residuals) &&
-        geo::rep_vjp_supported(*rep, device_inputs, device_residuals)) {
-        e = geo::launch_rep_residual(*rep, device_inputs, device_parameter, device_targets, device_residuals,
-                                     batch_size, stream);
-        if (e == cudaSuccess)
-            e = geo::launch_rep_vjp(*rep, device_inputs, device_residuals, batch_size, records, &ctas, stream);
+    if (rep != nullptr && geo::rep_sgd_supported(*rep, device_inputs, device_targets, device_residuals)) {
+        e = geo::launch_rep_mse_pass(*rep, device_inputs, device_parameter, device_targets, device_residuals,
+                                     batch_size, records, &ctas, stream);
     } else {
         e = geo::launch_cycle(*sp, geo::kCycle, device_inputs, device_targets, device_parameter, device_residuals,
                               batch_size, records, &ctas, stream);

@@ -195,13 +195,15 @@ struct TermParameter {
 };
 cudaError_t launch_rep_forward_terms(const RepDevice &rep, const double *inputs, const TermParameter &parameter,
                                      double *outputs, size_t batch, cudaStream_t stream);
-// residuals[s] = (x_s W or W x_s) - targets[s], the product computed with the
-// same arithmetic as launch_rep_forward (so targets equal to its outputs give
-// exactly zero); inputs, targets and residuals 16-byte aligned.
-bool rep_residual_supported(const RepDevice &rep, const double *inputs, const double *targets,
-                            const double *residuals);
-cudaError_t launch_rep_residual(const RepDevice &rep, const double *inputs, const double *parameter,
-                                const double *targets, double *residuals, size_t batch, cudaStream_t stream);
+// One pass of the MSE-SGD step: residuals[s] = (x_s W or W x_s) - targets[s],
+// the product computed with the arithmetic of launch_rep_forward (so targets
+// equal to its outputs give exactly zero), and the records of launch_rep_vjp
+// applied to those residuals (the same values, bit for bit); inputs, targets
+// and residuals 16-byte aligned.
+bool rep_sgd_supported(const RepDevice &rep, const double *inputs, const double *targets, const double *residuals);
+cudaError_t launch_rep_mse_pass(const RepDevice &rep, const double *inputs, const double *parameter,
+                                const double *targets, double *residuals, size_t batch, double *records,
+                                int *ctas_used, cudaStream_t stream);
 // Representation tables for (dimension, signature, side), built once and cached;
 // null when the algebra has no warp-specialised representation kernel (n < 5).
 const RepDevice *cached_rep_device(uint8_t dimension, const int8_t *signature, bool parameter_on_left);

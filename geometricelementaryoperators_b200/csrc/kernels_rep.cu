@@ -475,6 +475,114 @@ __device__ __forceinline__ void walsh(double (&w)[S]) {
             }
 }
 
+// A producer thread's blade group in the warp-specialised kernels (thread tid
+// handles group m = tid % D of the samples slot + SLOTS i, slot = tid / D):
+// raw offsets of the S member blades within a stage (roff), offsets of the S
+// kept entries in the ws_index layout (woff), and the sign masks of the gather
+// X'_f = out_f sum_t H[f][t] in_t x_t (and of its inverse).
+template <int D, int S>
+struct GroupMap {
+    int roff[S], woff[S];
+    unsigned in_sign[S], out_sign[S];
+    __device__ __forceinline__ GroupMap(const RepDevice &rep, int tid) {
+        using G = WsGeo<D, S>;
+        const int m = tid % D, slot = tid / D;
+        const int L = D == 8 ? (slot & 1) * 8 + m : m;
+#pragma unroll
+        for (int t = 0; t < S; ++t) {
+            roff[t] = slot * G::N + rep.ws_blade[L][t];
+            in_sign[t] = ((rep.ws_in_neg[L] >> t) & 1u) << 31;
+            const int r = rep.ws_out_row[L][t];
+            woff[t] = ws_index<D>(slot * S + r, rep.grp_col[m][r]);
+            out_sign[t] = ((rep.ws_out_neg[L] >> t) & 1u) << 31;
+        }
+    }
+};
+
+// W' = rho(W) (right) or rho(W)^T (left) of a dense parameter, built by the
+// whole CTA into shared memory (entry (k, j) sums the S blades A with
+// xm[A] = k ^ j, signed by the blade's sign and its Z mask on the column).
+template <int D, int N>
+__device__ __forceinline__ void build_wprime(const RepDevice &rep, const double *__restrict__ W, double *Wp) {
+    for (int idx = threadIdx.x; idx < D * D; idx += kWsThreads) {
+        const int k = idx / D, j = idx - k * D;
+        const int col = rep.side ? k : j;
+        double acc = 0.0;
+        for (int A = 0; A < N; ++A) {
+            if (rep.xm[A] != (k ^ j)) continue;
+            const double w = W[A];
+            const bool neg = (rep.sg[A] < 0) != ((__popc(rep.zm[A] & col) & 1) != 0);
+            acc += neg ? -w : w;
+        }
+        Wp[idx] = acc;
+    }
+}
+
+// Consumer-side G' accumulators of the warp-specialised kernels: D / 8
+// 8-column tiles of G', two k halves, the mma C fragment.
+template <int D>
+using GAcc = double[D / 8][2][D == 16 ? 4 : 2];
+
+// End of a warp-specialised training or VJP pass, called by every thread after
+// a __syncthreads (all stage memory free): reduces the consumer warps' G'
+// partials in warp order and the threads' sums of |R'|^2 (a fixed tree), and
+// writes the CTA's record: g_A = <G', rho(e_A)> / S, loss 0.5 sum |R'|^2 / S,
+// and the check value (NaN when some R' was not finite or a wait gave up).
+// rep_ws_kernel carries the same reduction, W' build and group tables inline:
+// moving them onto these helpers changes that kernel's register allocation,
+// and its timing is the measured one.
+template <int D, int S>
+__device__ __forceinline__ void ws_write_record(const RepDevice &rep, const GAcc<D> &gacc, double sq,
+                                                unsigned worst_exp, const unsigned *gave_up, double *scratch,
+                                                double *records) {
+    constexpr int N = D * S, PT = D / 8;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    double *Gs = scratch;                // 4 * D * D
+    double *Gsum = Gs + 4 * D * D;       // D * D
+    double *red = Gsum + D * D;          // kWsThreads
+    if (warp >= kWsProducers / 32) {
+        const int cw = warp - kWsProducers / 32;
+        const int g = lane >> 2, t4 = lane & 3;
+        double *gw = Gs + cw * D * D;
+#pragma unroll
+        for (int p = 0; p < PT; ++p)
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                gw[g * D + p * 8 + 2 * t4 + i] = gacc[p][0][i] + gacc[p][1][i];
+                if constexpr (D == 16) gw[(g + 8) * D + p * 8 + 2 * t4 + i] = gacc[p][0][2 + i] + gacc[p][1][2 + i];
+            }
+    }
+    red[tid] = sq;
+    const int bad = __syncthreads_or(worst_exp == 0x7ff00000u);
+    for (int idx = tid; idx < D * D; idx += kWsThreads)
+        Gsum[idx] = ((Gs[idx] + Gs[D * D + idx]) + Gs[2 * D * D + idx]) + Gs[3 * D * D + idx];
+    for (int width = kWsThreads / 2; width > 0; width >>= 1) {
+        __syncthreads();
+        if (tid < width) red[tid] += red[tid + width];
+    }
+    __syncthreads();
+    double *rec = records + (size_t)blockIdx.x * kRecStride;
+    const double inv_s = 1.0 / (double)S;  // exact: S is a power of two
+    if (tid < N) {
+        const int A = tid;
+        const int xa = rep.xm[A], za = rep.zm[A];
+        double acc = 0.0;
+        for (int j = 0; j < D; ++j) {
+            const double v = rep.side ? Gsum[j * D + (j ^ xa)] : Gsum[(j ^ xa) * D + j];
+            acc += (__popc(za & j) & 1) ? -v : v;
+        }
+        rec[A] = (rep.sg[A] < 0 ? -acc : acc) * inv_s;
+    }
+    if (tid == 0) {
+        rec[kRecLoss] = 0.5 * red[0] * inv_s;
+        rec[kRecCheckY] = 0.0;
+        // Y' = R' + T' with T' finite, so a non-finite output shows in R'.
+        rec[kRecCheckR] =
+            (bad || *(volatile const unsigned *)gave_up) ? __longlong_as_double(0x7ff8000000000000ll) : 0.0;
+        rec[kRecCheckIn] = 0.0;
+    }
+}
+
 // VJP = false: training pass (x, targets t, parameter W). VJP = true: parameter
 // VJP of given output cotangents c (in place of t, no W): the producers write
 // C' = P c instead of -T', and GEMM 1 is skipped (R' := C').
@@ -765,12 +873,11 @@ cudaError_t launch_rep_ws(const RepDevice &rep, const double *X, const double *T
 // is exact).
 //
 // Warps 0-3 (producers): thread 0 keeps FwdPipe::AHEAD bulk loads of raw x
-// tiles (and, with RESID, target tiles) in flight (completion on one mbarrier
-// per stage). For tile k all producers gather X' in place and arrive on
-// full[stage]; then, once the consumers have arrived on done[] for tile
-// k - FwdPipe::LAG, they scatter its Y' back to raw rows in place (with RESID
-// they store r = y - t there, y computed exactly as without), and thread 0
-// stores the tile's rows with one bulk copy. A stage is reloaded only after its
+// tiles in flight (completion on one mbarrier per stage). For tile k all
+// producers gather X' in place and arrive on full[stage]; then, once the
+// consumers have arrived on done[] for tile k - FwdPipe::LAG, they scatter its
+// Y' back to raw rows in place, and thread 0 stores the tile's rows with one
+// bulk copy. A stage is reloaded only after its
 // store has finished reading it (bulk wait_group.read).
 // Warps 4-7 (consumers): GEMM 1 transposed with W'^T fragments resident, as in
 // rep_ws_kernel, from zero accumulators; Y' is written over the X' rows the
@@ -791,19 +898,19 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
 
-template <int D, int S, bool RESID>
-__global__ void __launch_bounds__(kWsThreads, FwdPipe<RESID>::CTAS_PER_SM)
+template <int D, int S>
+__global__ void __launch_bounds__(kWsThreads, FwdPipe::CTAS_PER_SM)
 rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ W,
-               const TermParameter terms, const double *__restrict__ T, size_t batch, double *Y) {
+               const TermParameter terms, size_t batch, double *Y) {
     using G = WsGeo<D, S>;
-    using P = FwdPipe<RESID>;
+    using P = FwdPipe;
     constexpr int N = G::N, TS = G::TS, TILE = G::TILE;
-    constexpr int NST = P::STAGES, STAGE = P::ARRAYS * TILE;
+    constexpr int NST = P::STAGES, STAGE = TILE;
     constexpr int kConsumers = kWsThreads - kWsProducers;
     constexpr int kBarScatter = 1;  // named barrier of the producer warps
     extern __shared__ __align__(16) double smem[];
     double *Wp = smem;                      // D * D
-    double *stages = Wp + D * D;            // NST x (x tile [, target tile])
+    double *stages = Wp + D * D;            // NST x tiles
     uint64_t *loaded = reinterpret_cast<uint64_t *>(stages + NST * STAGE);
     uint64_t *full = loaded + NST;          // producers -> consumers: X' ready
     uint64_t *done = full + NST;            // consumers -> producers: Y' ready
@@ -871,9 +978,8 @@ rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
             size_t first;
             const unsigned bytes = (unsigned)tile_rows(k, &first) * N * (unsigned)sizeof(double);
             uint64_t *bar = &loaded[k % NST];
-            mbar_expect_tx(bar, P::ARRAYS * bytes);
+            mbar_expect_tx(bar, bytes);
             bulk_load(stages + (k % NST) * STAGE, X + first * N, bytes, bar);
-            if (RESID) bulk_load(stages + (k % NST) * STAGE + TILE, T + first * N, bytes, bar);
         };
         if (tid == 0)
             for (int k = 0; k < K && k < P::AHEAD; ++k) issue(k);
@@ -915,14 +1021,11 @@ rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
                 const int st = j % NST;
                 if (!mbar_wait(&done[st], (unsigned)((j / NST) & 1))) atomicOr(&s_gave_up, 1u);
                 double *xs = stages + st * STAGE;
-                double v[G::PER][S], tv[G::PER][S];
+                double v[G::PER][S];
 #pragma unroll
                 for (int i = 0; i < G::PER; ++i)
 #pragma unroll
-                    for (int f = 0; f < S; ++f) {
-                        v[i][f] = flip_sign(xs[G::SLOTS * i * N + woff[f]], out_sign[f]);
-                        tv[i][f] = RESID ? xs[TILE + G::SLOTS * i * N + roff[f]] : 0.0;  // raw target blade
-                    }
+                    for (int f = 0; f < S; ++f) v[i][f] = flip_sign(xs[G::SLOTS * i * N + woff[f]], out_sign[f]);
                 named_sync(kBarScatter, kWsProducers);  // every Y' read is done before the in-place writes
                 const bool poison = *(volatile unsigned *)&s_gave_up != 0u;
 #pragma unroll
@@ -930,11 +1033,9 @@ rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
                     walsh<S>(v[i]);
 #pragma unroll
                     for (int t = 0; t < S; ++t) {
-                        // y exactly as the plain forward computes it (the scaling by 1/S is exact);
-                        // with RESID the stored value is r = y - t.
+                        // the scaling by 1/S is exact (S is a power of two)
                         const double y = flip_sign(v[i][t], in_sign[t]) * inv_s;
-                        xs[G::SLOTS * i * N + roff[t]] =
-                            poison ? __longlong_as_double(0x7ff8000000000000ll) : (RESID ? __dsub_rn(y, tv[i][t]) : y);
+                        xs[G::SLOTS * i * N + roff[t]] = poison ? __longlong_as_double(0x7ff8000000000000ll) : y;
                     }
                 }
                 asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic writes -> bulk store
@@ -1009,14 +1110,14 @@ rep_fwd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
     }
 }
 
-template <int D, int S, bool RESID>
+template <int D, int S>
 cudaError_t launch_rep_fwd(const RepDevice &rep, const double *X, const double *W, const TermParameter &terms,
-                           const double *T, double *Y, size_t batch, cudaStream_t stream) {
+                           double *Y, size_t batch, cudaStream_t stream) {
     using G = WsGeo<D, S>;
-    using P = FwdPipe<RESID>;
+    using P = FwdPipe;
     if (rep.raw_stride != G::N || rep.D != D || rep.S != S) return cudaErrorInvalidValue;
-    auto kernel = rep_fwd_kernel<D, S, RESID>;
-    const size_t smem = (size_t)(D * D + P::STAGES * P::ARRAYS * G::TILE) * sizeof(double) +
+    auto kernel = rep_fwd_kernel<D, S>;
+    const size_t smem = (size_t)(D * D + P::STAGES * G::TILE) * sizeof(double) +
                         3 * P::STAGES * sizeof(uint64_t);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -1028,20 +1129,322 @@ cudaError_t launch_rep_fwd(const RepDevice &rep, const double *X, const double *
     size_t grid = (size_t)device_sm_count() * (size_t)per_sm;
     if (grid > tiles) grid = tiles;
     if (grid < 1) grid = 1;
-    kernel<<<(unsigned)grid, kWsThreads, smem, stream>>>(rep, X, W, terms, T, batch, Y);
+    kernel<<<(unsigned)grid, kWsThreads, smem, stream>>>(rep, X, W, terms, batch, Y);
     return cudaGetLastError();
 }
 
-template <bool RESID>
 cudaError_t launch_rep_forward_impl(const RepDevice &rep, const double *X, const double *W,
-                                    const TermParameter &terms, const double *T, double *Y, size_t batch,
-                                    cudaStream_t stream) {
-    if (!rep_forward_supported(rep, X, Y) || (RESID && ((uintptr_t)T & 15u) != 0u)) return cudaErrorInvalidValue;
-    if (rep.D == 16 && rep.S == 4) return launch_rep_fwd<16, 4, RESID>(rep, X, W, terms, T, Y, batch, stream);
-    if (rep.D == 8 && rep.S == 8) return launch_rep_fwd<8, 8, RESID>(rep, X, W, terms, T, Y, batch, stream);
-    if (rep.D == 8 && rep.S == 4) return launch_rep_fwd<8, 4, RESID>(rep, X, W, terms, T, Y, batch, stream);
-    if (rep.D == 16 && rep.S == 2) return launch_rep_fwd<16, 2, RESID>(rep, X, W, terms, T, Y, batch, stream);
+                                    const TermParameter &terms, double *Y, size_t batch, cudaStream_t stream) {
+    if (!rep_forward_supported(rep, X, Y)) return cudaErrorInvalidValue;
+    if (rep.D == 16 && rep.S == 4) return launch_rep_fwd<16, 4>(rep, X, W, terms, Y, batch, stream);
+    if (rep.D == 8 && rep.S == 8) return launch_rep_fwd<8, 8>(rep, X, W, terms, Y, batch, stream);
+    if (rep.D == 8 && rep.S == 4) return launch_rep_fwd<8, 4>(rep, X, W, terms, Y, batch, stream);
+    if (rep.D == 16 && rep.S == 2) return launch_rep_fwd<16, 2>(rep, X, W, terms, Y, batch, stream);
     return cudaErrorInvalidValue;
+}
+
+// ---------------------------------------------------------------------------
+// Fused MSE-SGD pass (16-byte aligned x, t and r): the reference device ABI's
+// forward -> r = y - t (stored) -> 0.5 r^2 -> parameter VJP of r
+// (src/batch_gp_cuda.cu:152-196) in one pass over x and t. Per tile:
+//   producers, gather phase: X' = P x in place, as rep_fwd_kernel;
+//   consumers, GEMM 1: Y' = X' W' (W'^T fragments resident) into the stage's
+//     third tile;
+//   producers, residual phase: y = P^-1 Y' exactly as rep_fwd_kernel computes
+//     it, r = y - t over the raw target rows in place (one bulk copy stores
+//     them), and R' = P r from the same registers into the third tile, as
+//     rep_ws_kernel<VJP> gathers its cotangents;
+//   consumers, GEMM 2: G' += X'^T R' and the sum of |R'|^2, as rep_ws_kernel<VJP>.
+// y is computed by the same operations as rep_fwd_kernel and R' as
+// rep_ws_kernel<VJP> computes it from a stored r, on the grid of that kernel,
+// so the residuals are bitwise the forward's outputs minus t and the records
+// bitwise those of the parameter VJP of the stored residuals, while x is read
+// once and r is never read back.
+// Handoffs (mbarriers, one phase per tile of a stage): loaded (bulk loads),
+// full (X'), done (Y'), resid (R' and r), freed (GEMM 2 has read the stage;
+// producer thread 0 waits on it before reloading the stage, together with
+// bulk wait_group.read for the residual store). Every wait is bounded; a wait
+// that gives up poisons the CTA's remaining residuals and its record.
+template <int D, int S>
+__global__ void __launch_bounds__(kWsThreads, SgdPipe::CTAS_PER_SM)
+rep_sgd_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ T,
+               const double *__restrict__ W, size_t batch, double *R, double *__restrict__ records) {
+    using G = WsGeo<D, S>;
+    using P = SgdPipe;
+    constexpr int N = G::N, TS = G::TS, TILE = G::TILE;
+    constexpr int NST = P::STAGES, STAGE = P::ARRAYS * TILE;
+    constexpr int kConsumers = kWsThreads - kWsProducers;
+    constexpr int kBarProducers = 1;  // named barrier of the producer warps
+    static_assert(5 * D * D + kWsThreads <= NST * STAGE, "epilogue scratch fits");
+    extern __shared__ __align__(16) double smem[];
+    double *Wp = smem;                      // D * D
+    double *stages = Wp + D * D;            // NST x (x tile, target tile, Y'/R' tile)
+    uint64_t *loaded = reinterpret_cast<uint64_t *>(stages + NST * STAGE);
+    uint64_t *full = loaded + NST;
+    uint64_t *done = full + NST;
+    uint64_t *resid = done + NST;
+    uint64_t *freed = resid + NST;
+    __shared__ unsigned s_gave_up;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t tiles = (batch + TS - 1) / TS;
+    const int K = (size_t)blockIdx.x < tiles ? (int)((tiles - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+
+    if (tid == 0) {
+        for (int s = 0; s < NST; ++s) {
+            mbar_init(&loaded[s], 1);
+            mbar_init(&full[s], kWsProducers);
+            mbar_init(&done[s], kConsumers);
+            mbar_init(&resid[s], kWsProducers);
+            mbar_init(&freed[s], kConsumers);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        s_gave_up = 0u;
+    }
+    build_wprime<D, N>(rep, W, Wp);
+    __syncthreads();
+
+    constexpr int PT = D / 8;
+    GAcc<D> gacc;
+#pragma unroll
+    for (int p = 0; p < PT; ++p)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int i = 0; i < (D == 16 ? 4 : 2); ++i) gacc[p][h][i] = 0.0;
+    double sq = 0.0;
+    unsigned worst_exp = 0u;
+
+    if (warp < kWsProducers / 32) {
+        // ------------------------------------------------------------ producers
+        const int slot = tid / D;
+        const GroupMap<D, S> gm(rep, tid);
+        const double inv_s = 1.0 / (double)S;  // exact: S is a power of two
+        auto tile_rows = [&](int k, size_t *first) {
+            *first = (blockIdx.x + (size_t)k * gridDim.x) * TS;
+            return batch - *first < (size_t)TS ? (int)(batch - *first) : TS;
+        };
+        auto issue = [&](int k) {
+            size_t first;
+            const unsigned bytes = (unsigned)tile_rows(k, &first) * N * (unsigned)sizeof(double);
+            uint64_t *bar = &loaded[k % NST];
+            double *dst = stages + (k % NST) * STAGE;
+            mbar_expect_tx(bar, 2u * bytes);
+            bulk_load(dst, X + first * N, bytes, bar);
+            bulk_load(dst + TILE, T + first * N, bytes, bar);
+        };
+        if (tid == 0)
+            for (int k = 0; k < K && k < P::AHEAD; ++k) issue(k);
+        for (int k = 0; k < K + P::LAG; ++k) {
+            if (k < K) {
+                // gather phase of tile k
+                const int st = k % NST;
+                if (!mbar_wait(&loaded[st], (unsigned)((k / NST) & 1))) atomicOr(&s_gave_up, 1u);
+                size_t first;
+                const int valid = tile_rows(k, &first);
+                double *xs = stages + st * STAGE;
+                double v[G::PER][S];
+#pragma unroll
+                for (int i = 0; i < G::PER; ++i) {
+                    const bool ok = slot + G::SLOTS * i < valid;
+#pragma unroll
+                    for (int t = 0; t < S; ++t) v[i][t] = ok ? xs[G::SLOTS * i * N + gm.roff[t]] : 0.0;
+                }
+                named_sync(kBarProducers, kWsProducers);  // every raw read is done before the in-place writes
+#pragma unroll
+                for (int i = 0; i < G::PER; ++i) {
+#pragma unroll
+                    for (int t = 0; t < S; ++t) v[i][t] = flip_sign(v[i][t], gm.in_sign[t]);
+                    walsh<S>(v[i]);
+#pragma unroll
+                    for (int f = 0; f < S; ++f)
+                        xs[G::SLOTS * i * N + gm.woff[f]] = flip_sign(v[i][f], gm.out_sign[f]);
+                }
+                mbar_arrive(&full[st]);
+            }
+            const int j = k - P::LAG;
+            if (j >= 0) {
+                // residual phase of tile j: every access below is to this thread's own
+                // kept entries (woff) and raw blades (roff), so reads and in-place writes
+                // need no barrier between them
+                const int st = j % NST;
+                if (!mbar_wait(&done[st], (unsigned)((j / NST) & 1))) atomicOr(&s_gave_up, 1u);
+                size_t first;
+                const int valid = tile_rows(j, &first);
+                double *ts = stages + st * STAGE + TILE;
+                double *ys = ts + TILE;
+                const bool poison = *(volatile unsigned *)&s_gave_up != 0u;
+#pragma unroll
+                for (int i = 0; i < G::PER; ++i) {
+                    const bool ok = slot + G::SLOTS * i < valid;
+                    double v[S];
+#pragma unroll
+                    for (int f = 0; f < S; ++f) v[f] = flip_sign(ys[G::SLOTS * i * N + gm.woff[f]], gm.out_sign[f]);
+                    walsh<S>(v);
+#pragma unroll
+                    for (int t = 0; t < S; ++t) {
+                        const int at = G::SLOTS * i * N + gm.roff[t];
+                        // y exactly as the plain forward computes it (the scaling by 1/S is
+                        // exact); rows past the batch contribute zero residuals
+                        const double y = flip_sign(v[t], gm.in_sign[t]) * inv_s;
+                        double r = ok ? __dsub_rn(y, ts[at]) : 0.0;
+                        if (poison) r = __longlong_as_double(0x7ff8000000000000ll);
+                        ts[at] = r;
+                        v[t] = flip_sign(r, gm.in_sign[t]);
+                    }
+                    walsh<S>(v);
+#pragma unroll
+                    for (int f = 0; f < S; ++f) ys[G::SLOTS * i * N + gm.woff[f]] = flip_sign(v[f], gm.out_sign[f]);
+                }
+                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic writes -> bulk store
+                mbar_arrive(&resid[st]);
+                named_sync(kBarProducers, kWsProducers);  // every residual is written before the store
+                if (tid == 0) bulk_store(R + first * N, ts, (unsigned)valid * N * (unsigned)sizeof(double));
+            }
+            const int ahead = k + P::AHEAD;
+            if (tid == 0 && ahead < K) {
+                // The stage of `ahead` last held tile ahead - NST: its GEMM 2 is done and
+                // its residual store (STORE_PENDING stores ago at most) has read it.
+                const int prev = ahead - NST;
+                if (prev >= 0) {
+                    if (!mbar_wait(&freed[prev % NST], (unsigned)((prev / NST) & 1))) atomicOr(&s_gave_up, 1u);
+                    bulk_wait_read<P::STORE_PENDING>();
+                }
+                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                issue(ahead);
+            }
+        }
+        if (tid == 0) {
+            asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+            // After a wait that gave up, bounded waits for loads that may still be in flight.
+            if (*(volatile unsigned *)&s_gave_up != 0u)
+                for (int k = K > NST ? K - NST : 0; k < K; ++k)
+                    (void)mbar_wait(&loaded[k % NST], (unsigned)((k / NST) & 1));
+        }
+    } else {
+        // ------------------------------------------------------------ consumers
+        const int cw = warp - kWsProducers / 32;
+        const int g = lane >> 2, t4 = lane & 3;
+        constexpr int KT = D / 4;
+        double wa[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (D == 16) wa[i] = Wp[(t4 + 4 * (i / 2)) * D + g + 8 * (i % 2)];
+            else wa[i] = i < KT ? Wp[(4 * i + t4) * D + g] : 0.0;
+        }
+        for (int k = 0; k < K + P::LAG; ++k) {
+            if (k < K) {
+                // GEMM 1 of tile k: Y' into the third tile
+                const int st = k % NST;
+                if (!mbar_wait(&full[st], (unsigned)((k / NST) & 1))) atomicOr(&s_gave_up, 1u);
+                const double *xs = stages + st * STAGE;
+                double *ys = stages + st * STAGE + 2 * TILE;
+#pragma unroll
+                for (int jj = 0; jj < G::GPW; jj += 2) {
+                    int n0[2];
+                    n0[0] = (cw * G::GPW + jj) * 8;
+                    n0[1] = n0[0] + 8;
+                    if constexpr (D == 16) {
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) {
+                            double b[4], c[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk) b[kk] = xs[ws_index<D>(n0[q] + g, 4 * kk + t4)];
+                            mma_16x8x16(c, wa, b);
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                ys[ws_index<D>(n0[q] + 2 * t4 + h, g)] = c[h];
+                                ys[ws_index<D>(n0[q] + 2 * t4 + h, g + 8)] = c[2 + h];
+                            }
+                        }
+                    } else {
+                        double c[2][2] = {{0.0, 0.0}, {0.0, 0.0}};
+#pragma unroll
+                        for (int kk = 0; kk < KT; ++kk)
+#pragma unroll
+                            for (int q = 0; q < 2; ++q) mma_8x8x4(c[q], wa[kk], xs[ws_index<D>(n0[q] + g, 4 * kk + t4)]);
+#pragma unroll
+                        for (int q = 0; q < 2; ++q)
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) ys[ws_index<D>(n0[q] + 2 * t4 + h, g)] = c[q][h];
+                    }
+                }
+                mbar_arrive(&done[st]);
+            }
+            const int j = k - P::LAG;
+            if (j >= 0) {
+                // GEMM 2 of tile j on X' and R', in the order of rep_ws_kernel<VJP>
+                const int st = j % NST;
+                if (!mbar_wait(&resid[st], (unsigned)((j / NST) & 1))) atomicOr(&s_gave_up, 1u);
+                const double *xs = stages + st * STAGE;
+                const double *rs = xs + 2 * TILE;
+#pragma unroll
+                for (int jj = 0; jj < G::GPW; jj += 2) {
+                    int n0[2];
+                    n0[0] = (cw * G::GPW + jj) * 8;
+                    n0[1] = n0[0] + 8;
+                    if constexpr (D == 16) {
+                        double ax[8], rlo[4], rhi[4];
+#pragma unroll
+                        for (int m = 0; m < 4; ++m) {
+                            const int row = n0[m >> 1] + 2 * t4 + (m & 1);
+                            const int plo = ws_index<D>(row, g), phi = ws_index<D>(row, g + 8);
+                            rlo[m] = rs[plo];
+                            rhi[m] = rs[phi];
+                            sq = fma(rlo[m], rlo[m], sq);
+                            sq = fma(rhi[m], rhi[m], sq);
+                            worst_exp = max(worst_exp, max(exponent_bits(rlo[m]), exponent_bits(rhi[m])));
+                            ax[2 * m] = xs[plo];
+                            ax[2 * m + 1] = xs[phi];
+                        }
+                        mma_16x8x16(gacc[0][0], ax, rlo);
+                        mma_16x8x16(gacc[PT - 1][0], ax, rhi);
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 2; ++q)
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const int pos = ws_index<D>(n0[q] + 2 * t4 + h, g);
+                                const double r = rs[pos];
+                                sq = fma(r, r, sq);
+                                worst_exp = max(worst_exp, exponent_bits(r));
+                                mma_8x8x4(gacc[0][h], xs[pos], r);
+                            }
+                    }
+                }
+                mbar_arrive(&freed[st]);
+            }
+        }
+    }
+    __syncthreads();
+    ws_write_record<D, S>(rep, gacc, sq, worst_exp, &s_gave_up, stages, records);
+}
+
+template <int D, int S>
+cudaError_t launch_rep_sgd(const RepDevice &rep, const double *X, const double *T, const double *W, double *R,
+                           size_t batch, double *records, int *ctas_used, cudaStream_t stream) {
+    using G = WsGeo<D, S>;
+    using P = SgdPipe;
+    if (rep.raw_stride != G::N || rep.D != D || rep.S != S) return cudaErrorInvalidValue;
+    auto kernel = rep_sgd_kernel<D, S>;
+    const size_t smem = (size_t)(D * D + P::STAGES * P::ARRAYS * G::TILE) * sizeof(double) +
+                        5 * P::STAGES * sizeof(uint64_t);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kWsThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    // The grid of launch_rep_ws (two CTAs per SM there too), so that the records
+    // partition the batch as the parameter VJP's do.
+    const size_t tiles = (batch + G::TS - 1) / G::TS;
+    size_t grid = (size_t)device_sm_count() * (size_t)per_sm;
+    if (grid > (size_t)kMaxCtas) grid = kMaxCtas;
+    if (grid > tiles) grid = tiles;
+    if (grid < 1) grid = 1;
+    kernel<<<(unsigned)grid, kWsThreads, smem, stream>>>(rep, X, T, W, batch, R, records);
+    if (ctas_used) *ctas_used = (int)grid;
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -1056,26 +1459,13 @@ cudaError_t launch_rep_forward(const RepDevice &rep, const double *X, const doub
     TermParameter none;
     none.terms = 0;
     none.values = nullptr;
-    return launch_rep_forward_impl<false>(rep, X, W, none, nullptr, Y, batch, stream);
+    return launch_rep_forward_impl(rep, X, W, none, Y, batch, stream);
 }
 
 cudaError_t launch_rep_forward_terms(const RepDevice &rep, const double *X, const TermParameter &terms, double *Y,
                                      size_t batch, cudaStream_t stream) {
     if (terms.terms < 1 || terms.terms > 64) return cudaErrorInvalidValue;
-    return launch_rep_forward_impl<false>(rep, X, nullptr, terms, nullptr, Y, batch, stream);
-}
-
-bool rep_residual_supported(const RepDevice &rep, const double *X, const double *T, const double *R) {
-    return rep_forward_supported(rep, X, R) && ((uintptr_t)T & 15u) == 0u;
-}
-
-cudaError_t launch_rep_residual(const RepDevice &rep, const double *X, const double *W, const double *T, double *R,
-                                size_t batch, cudaStream_t stream) {
-    if (W == nullptr || T == nullptr) return cudaErrorInvalidValue;
-    TermParameter none;
-    none.terms = 0;
-    none.values = nullptr;
-    return launch_rep_forward_impl<true>(rep, X, W, none, T, R, batch, stream);
+    return launch_rep_forward_impl(rep, X, nullptr, terms, Y, batch, stream);
 }
 
 cudaError_t launch_rep_cycle(const RepDevice &rep, const double *X, const double *T, const double *W, size_t batch,
@@ -1093,6 +1483,20 @@ cudaError_t launch_rep_cycle(const RepDevice &rep, const double *X, const double
     return cudaErrorInvalidValue;
 }
 
+
+bool rep_sgd_supported(const RepDevice &rep, const double *X, const double *T, const double *R) {
+    return rep.ws_ready && rep_supported(rep) && (((uintptr_t)X | (uintptr_t)T | (uintptr_t)R) & 15u) == 0u;
+}
+
+cudaError_t launch_rep_mse_pass(const RepDevice &rep, const double *X, const double *W, const double *T, double *R,
+                                size_t batch, double *records, int *ctas_used, cudaStream_t stream) {
+    if (W == nullptr || !rep_sgd_supported(rep, X, T, R)) return cudaErrorInvalidValue;
+    if (rep.D == 16 && rep.S == 4) return launch_rep_sgd<16, 4>(rep, X, T, W, R, batch, records, ctas_used, stream);
+    if (rep.D == 8 && rep.S == 8) return launch_rep_sgd<8, 8>(rep, X, T, W, R, batch, records, ctas_used, stream);
+    if (rep.D == 8 && rep.S == 4) return launch_rep_sgd<8, 4>(rep, X, T, W, R, batch, records, ctas_used, stream);
+    if (rep.D == 16 && rep.S == 2) return launch_rep_sgd<16, 2>(rep, X, T, W, R, batch, records, ctas_used, stream);
+    return cudaErrorInvalidValue;
+}
 
 bool rep_vjp_supported(const RepDevice &rep, const double *X, const double *C) {
     return rep.ws_ready && rep_supported(rep) && (((uintptr_t)X | (uintptr_t)C) & 15u) == 0u;

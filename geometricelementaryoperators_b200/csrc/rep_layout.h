@@ -19,21 +19,38 @@ constexpr int kWsStages = 6;       // shared-memory stages per CTA
 
 // Forward kernel (rep_fwd_kernel): a stage holds one x tile (8 KB), which is
 // gathered in place, overwritten by Y', scattered back to raw y rows and
-// stored from the same stage; with RESID the stage also holds the target tile
-// and the kernel stores r = y - t.
-template <bool RESID>
+// stored from the same stage.
 struct FwdPipe {
-    static constexpr int ARRAYS = RESID ? 2 : 1;  // x tile (+ target tile) per stage
-    static constexpr int STAGES = RESID ? 6 : 8;  // shared-memory stages per CTA
-    static constexpr int AHEAD = RESID ? 3 : 4;   // tiles whose bulk loads are in flight
-    // CTAs per SM (the plain forward's 66 KB ring fits three; measured faster
-    // than 12 stages at two CTAs per SM)
-    static constexpr int CTAS_PER_SM = RESID ? 2 : 3;
-    static constexpr int LAG = 2;                 // the scatter of tile k - LAG follows the gather of tile k
+    static constexpr int STAGES = 8;        // shared-memory stages per CTA
+    static constexpr int AHEAD = 4;         // tiles whose bulk loads are in flight
+    // CTAs per SM (the 66 KB ring fits three; measured faster than 12 stages at
+    // two CTAs per SM)
+    static constexpr int CTAS_PER_SM = 3;
+    static constexpr int LAG = 2;           // the scatter of tile k - LAG follows the gather of tile k
     // Bulk stores that may still be reading shared memory when a stage is
     // reloaded: the load of tile k + AHEAD reuses the stage of tile
     // k + AHEAD - STAGES, whose store was issued this many stores ago.
     static constexpr int STORE_PENDING = STAGES - 1 - LAG - AHEAD;
+    static_assert(STORE_PENDING >= 0, "a stage is reloaded only after its store was issued");
+};
+
+// Fused MSE-SGD pass (rep_sgd_kernel): a stage holds the x tile (gathered to
+// X' in place), the target tile (replaced in place by r = y - t, which a bulk
+// copy stores) and a third tile that takes Y' from the consumers and then
+// R' = P r from the producers. Iteration k of the producers gathers tile k,
+// runs the residual phase of tile k - LAG and then issues the loads of tile
+// k + AHEAD; iteration k of the consumers runs GEMM 1 of tile k and GEMM 2 of
+// tile k - LAG.
+struct SgdPipe {
+    static constexpr int ARRAYS = 3;
+    static constexpr int STAGES = 4;       // 24 KB stages: two CTAs per SM
+    static constexpr int AHEAD = 2;        // tiles whose bulk loads are in flight
+    static constexpr int LAG = 1;
+    static constexpr int CTAS_PER_SM = 2;
+    // The load of tile k + AHEAD (issued at the end of iteration k) reuses the
+    // stage of tile k + AHEAD - STAGES, whose residual store was issued in
+    // iteration k + AHEAD - STAGES + LAG: this many stores ago at most.
+    static constexpr int STORE_PENDING = STAGES - AHEAD - LAG;
     static_assert(STORE_PENDING >= 0, "a stage is reloaded only after its store was issued");
 };
 

@@ -96,15 +96,14 @@ static const char *check_ws_layout(const RepDevice &dev) {
     return nullptr;
 }
 
-// The forward kernel's pipeline (rep_fwd_kernel, both FwdPipe variants):
+// The forward kernel's pipeline (rep_fwd_kernel, FwdPipe):
 // producer iteration k issues the load of tile k + AHEAD (after waiting until
 // at most STORE_PENDING bulk stores are pending), gathers tile k and scatters
 // + stores tile k - LAG. Replays the order for many tile counts and checks that
 // every load goes into a stage whose previous tile was already stored, and
 // that the stores still pending at that moment are all later tiles.
-template <bool RESID>
 static const char *check_forward_pipeline() {
-    using P = FwdPipe<RESID>;
+    using P = FwdPipe;
     for (int K = 1; K <= 64; ++K) {
         std::vector<int> stored;  // tiles in store-issue order
         std::vector<bool> issued(K, false);
@@ -131,6 +130,117 @@ static const char *check_forward_pipeline() {
             if (j >= 0 && j < K) stored.push_back(j);
         }
         if ((int)stored.size() != K) return "not every tile stored";
+    }
+    return nullptr;
+}
+
+// Replays the handoffs of the fused MSE-SGD kernel (SgdPipe) for every tile
+// count up to 64 as two agents (the producer warps, with thread 0's loads and
+// stores, and the consumer warps), each blocking exactly where the kernel
+// waits. Two schedules are replayed: producers run as far as they can before
+// the consumers move, and the reverse. Checks: no deadlock; every phase finds
+// its stage holding its own tile (so no mbarrier phase of a stage is overtaken
+// by a later tile before its wait); a stage is reloaded only after GEMM 2 of
+// its previous tile and after the residual store reading it has been retired
+// by wait_group.read (stores retire only when a wait forces them).
+static const char *check_sgd_pipeline() {
+    using P = SgdPipe;
+    const int NST = P::STAGES;
+    for (int K = 1; K <= 64; ++K) {
+        for (int policy = 0; policy < 2; ++policy) {
+            std::vector<int> issued(K, 0), full(K, 0), done(K, 0), resid(K, 0), freed(K, 0);
+            std::vector<int> stores;  // tiles whose residual store may still read shared memory
+            std::vector<int> stage_tile(NST, -1);
+            int pk = 0, pphase = 0;   // producer iteration; phase 0 gather, 1 residual, 2 issue
+            int ck = 0, cphase = 0;   // consumer iteration; phase 0 GEMM 1, 1 GEMM 2
+            for (int k = 0; k < K && k < P::AHEAD; ++k) {
+                issued[k] = 1;
+                stage_tile[k % NST] = k;
+            }
+            auto owns = [&](int tile) { return stage_tile[tile % NST] == tile; };
+            // 1 progressed, 0 blocked, -1 finished, -2 stage misuse
+            auto producer_step = [&]() -> int {
+                if (pk >= K + P::LAG) return -1;
+                if (pphase == 0) {
+                    if (pk < K) {
+                        if (!issued[pk]) return 0;
+                        if (!owns(pk)) return -2;
+                        full[pk] = 1;
+                    }
+                    pphase = 1;
+                    return 1;
+                }
+                if (pphase == 1) {
+                    const int j = pk - P::LAG;
+                    if (j >= 0) {
+                        if (!done[j]) return 0;
+                        if (!owns(j)) return -2;
+                        resid[j] = 1;
+                        stores.push_back(j);
+                    }
+                    pphase = 2;
+                    return 1;
+                }
+                const int ahead = pk + P::AHEAD;
+                if (ahead < K) {
+                    const int prev = ahead - NST;
+                    if (prev >= 0) {
+                        if (!freed[prev]) return 0;
+                        // wait_group.read STORE_PENDING retires all but the newest STORE_PENDING stores
+                        while ((int)stores.size() > P::STORE_PENDING) stores.erase(stores.begin());
+                        for (int s : stores)
+                            if (s % NST == ahead % NST) return -2;  // a store still reads the stage
+                    }
+                    issued[ahead] = 1;
+                    stage_tile[ahead % NST] = ahead;
+                }
+                ++pk;
+                pphase = 0;
+                return 1;
+            };
+            auto consumer_step = [&]() -> int {
+                if (ck >= K + P::LAG) return -1;
+                if (cphase == 0) {
+                    if (ck < K) {
+                        if (!full[ck]) return 0;
+                        if (!owns(ck)) return -2;
+                        done[ck] = 1;
+                    }
+                    cphase = 1;
+                    return 1;
+                }
+                const int j = ck - P::LAG;
+                if (j >= 0) {
+                    if (!resid[j]) return 0;
+                    if (!owns(j)) return -2;
+                    freed[j] = 1;
+                }
+                ++ck;
+                cphase = 0;
+                return 1;
+            };
+            for (;;) {
+                int a, b;
+                if (policy == 0) {
+                    while ((a = producer_step()) == 1) {}
+                    b = consumer_step();
+                } else {
+                    while ((b = consumer_step()) == 1) {}
+                    a = producer_step();
+                }
+                if (a == -2 || b == -2) return "a stage was used by a tile that does not own it";
+                if (a == -1 && b == -1) break;
+                if (a != 1 && b != 1) {
+                    a = producer_step();
+                    b = consumer_step();
+                    if (a == -2 || b == -2) return "a stage was used by a tile that does not own it";
+                    if (a == -1 && b == -1) break;
+                    if (a != 1 && b != 1) return "deadlock";
+                }
+            }
+            for (int k = 0; k < K; ++k)
+                if (!freed[k] || !resid[k]) return "not every tile completed";
+        }
     }
     return nullptr;
 }
@@ -175,12 +285,12 @@ int main() {
     std::mt19937_64 rng(5);
     std::uniform_real_distribution<double> U(-1.0, 1.0);
     int cases = 0;
-    if (const char *why = check_forward_pipeline<false>()) {
+    if (const char *why = check_forward_pipeline()) {
         printf("FAIL forward pipeline: %s\n", why);
         return 1;
     }
-    if (const char *why = check_forward_pipeline<true>()) {
-        printf("FAIL residual pipeline: %s\n", why);
+    if (const char *why = check_sgd_pipeline()) {
+        printf("FAIL mse-sgd pipeline: %s\n", why);
         return 1;
     }
     for (int n = 1; n <= 6; ++n) {

@@ -273,6 +273,57 @@ def test_full_size_n6_properties(oracle, q):
         assert host(dloss)[0] == 0.0 and np.all(host(dgrad) == 0.0) and np.array_equal(host(dparam), w)
 
 
+@pytest.mark.parametrize("batch", [1, 17, 33, 1000, 4099, 296 * 16 * 3 + 5, (1 << 22) + 5])
+def test_sgd_step_is_residual_then_vjp(oracle, batch):
+    """The device MSE-SGD step at n = 5, 6 (one fused pass): its residuals are
+    bitwise the planned forward's outputs minus the targets (one IEEE
+    subtraction each), its gradient is bitwise the parameter VJP entry point
+    applied to those residuals, and loss and update match the oracle (small
+    batches: the whole batch; the full-size batch: spot rows, the loss of the
+    stored residuals and the update rule)."""
+    import torch
+
+    L = _lib()
+    big = batch > 1 << 20
+    cases = [(6, 0), (6, 3)] if big else [(n, q) for n in (5, 6) for q in range(n + 1)]
+    for n, q in cases:
+        sig = canonical_signature(n, q)
+        plan = CudaPlan(sig)
+        N = 1 << n
+        gen = torch.Generator(device="cuda").manual_seed(77 * n + q + batch)
+        X = torch.rand((batch, N), dtype=torch.float64, device="cuda", generator=gen) * 2 - 1
+        T = torch.rand((batch, N), dtype=torch.float64, device="cuda", generator=gen) * 2 - 1
+        w = splitmix_uniform(600 + 7 * n + q, (N,)) * 0.35
+        dw = dev(w)
+        for left in ((q % 2,) if big else (0, 1)):
+            Y = torch.empty_like(X)
+            assert L.geo_batch_gp_cuda_planned_forward_f64(ctypes.byref(plan.dev), ptr(X), batch, ptr(dw), left,
+                                                           ptr(Y), stream()) == 0
+            res = torch.full_like(X, 3.0)
+            dparam, dgrad, dloss = dev(w.copy()), dev(np.zeros(N)), dev(np.zeros(1))
+            assert L.geo_batch_gp_cuda_mse_sgd_step_f64(ctypes.byref(plan.dev), ptr(X), ptr(T), batch, 1e-3, left,
+                                                        ptr(dparam), ptr(res), ptr(dgrad), ptr(dloss), stream()) == 0
+            g_vjp = dev(np.zeros(N))
+            assert L.geo_batch_gp_cuda_parameter_vjp_f64(ctypes.byref(plan.dev), ptr(X), ptr(res), batch, left,
+                                                         ptr(g_vjp), stream()) == 0
+            sync()
+            assert torch.equal(res, Y - T), (n, q, left)
+            assert np.array_equal(host(dgrad), host(g_vjp)), (n, q, left)
+            if not big:
+                st, w_ref, mean_loss = oracle.sgd_step(sig, host(X), host(T), 1e-3, w, bool(left))
+                assert st == 0
+                assert tol_close(host(dloss)[0] / batch, mean_loss, TOL)
+                assert tol_close(host(dparam), w_ref, TOL), (n, q, left, max_violation(host(dparam), w_ref, TOL))
+            else:
+                rows = np.concatenate([np.random.default_rng(batch + q).integers(0, batch, 256),
+                                       np.arange(batch - 20, batch)])
+                idx = torch.as_tensor(rows, device="cuda")
+                y_ref = oracle.forward(sig, host(X[idx]), w, bool(left))[1]
+                assert tol_close(host(res[idx]), y_ref - host(T[idx]), TOL)
+                assert tol_close(host(dloss)[0], 0.5 * float((res * res).sum()), TOL)
+                assert np.array_equal(host(dparam), w - (1e-3 / batch) * host(dgrad))
+
+
 def accurate_vjp(oracle, sig, x, cot, left: bool) -> np.ndarray:
     """g_p = sum_i sigma(i,p) (X^T C)[i][i^p] with X^T C formed per 1024-sample chunk in
     float64 and accumulated across chunks in extended precision (about 1e-15
