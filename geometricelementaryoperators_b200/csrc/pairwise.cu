@@ -492,9 +492,7 @@ constexpr int kF64StageBoxes = 8;              // a: 4 boxes, b: 4 boxes
 // (accumulating launches) 32 per-lane slots of 16 doubles at an 18-double
 // stride (16-byte aligned, conflict-free 16-byte writes); 5 KB keeps every box
 // on the 1024-byte period of the swizzle.
-constexpr int kF64OutArea = 640;                  // doubles per compute warp (5 KB)
-constexpr int kF64SlotStride = 18;                // doubles between the lanes' slots
-static_assert(kF64Rows * kF64SlotStride <= kF64OutArea && kF64Box <= kF64OutArea, "output area");
+constexpr int kF64OutArea = kF64Box;              // doubles per compute warp (one output box, 4 KB)
 constexpr size_t kF64Smem =
     ((size_t)kF64Stages * kF64StageBoxes * kF64Box + (size_t)kF64Compute * kF64OutArea) * sizeof(double) + 1024;
 
@@ -553,14 +551,15 @@ __device__ __forceinline__ void f64_wait(uint64_t *bar, unsigned parity) {
     atomicAdd(&g_pairwise_tma_wait_failures, 1u);
 }
 
+// products = 1: y = a b. products = 2 (the JVP): y = a b + a2 b2 in one pass;
+// the ring alternates (a, b) and (a2, b2) tiles of the same rows and the
+// compute warps keep one accumulator across both before the single store.
 template <int NEG>
 __global__ void __launch_bounds__(kF64Threads, 2)
 pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                           const __grid_constant__ CUtensorMap map_a2, const __grid_constant__ CUtensorMap map_b2,
                            const __grid_constant__ CUtensorMap map_out, const F64BlockSigns signs, size_t batch,
-                           double *acc_out) {
-    // acc_out == null: outputs are stored (TMA tensor store of a swizzled box).
-    // acc_out != null: outputs are added into acc_out[batch][64] by a bulk
-    // reduce-add per row (one rounding per element), for the JVP's second product.
+                           int products) {
     extern __shared__ unsigned char f64_raw[];
     __shared__ __align__(8) uint64_t full[kF64Stages], empty[kF64Stages];
     __shared__ F64BlockSigns sgn;
@@ -582,19 +581,23 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
     if (warp == kF64Compute) {
         // ---- producer: one thread keeps the ring full
         if (lane == 0) {
-            for (int k = 0; k < K; ++k) {
-                const int s = k % kF64Stages;
-                // the stage last held tile k - kF64Stages: wait until all compute warps released it
-                if (k >= kF64Stages) f64_wait(&empty[s], (unsigned)((k / kF64Stages - 1) & 1));
+            // stage loads v = 0, 1, ...: tile v / products, operand pair v % products
+            for (int v = 0; v < K * products; ++v) {
+                const int s = v % kF64Stages;
+                // the stage last held load v - kF64Stages: wait until all compute warps released it
+                if (v >= kF64Stages) f64_wait(&empty[s], (unsigned)((v / kF64Stages - 1) & 1));
                 double *st = base + s * kF64StageBoxes * kF64Box;
-                const int y = (int)((blockIdx.x + (size_t)k * gridDim.x) * kF64Rows);
+                const int y = (int)((blockIdx.x + (size_t)(v / products) * gridDim.x) * kF64Rows);
+                const bool second = v % products != 0;
+                const CUtensorMap *ma = second ? &map_a2 : &map_a;
+                const CUtensorMap *mb = second ? &map_b2 : &map_b;
                 asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
                 asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(&full[s])),
                              "r"((unsigned)(kF64StageBoxes * kF64Box * sizeof(double)))
                              : "memory");
                 for (int c = 0; c < 4; ++c) {
-                    tma_load_2d(st + c * kF64Box, &map_a, 16 * c, y, &full[s]);
-                    tma_load_2d(st + (4 + c) * kF64Box, &map_b, 16 * c, y, &full[s]);
+                    tma_load_2d(st + c * kF64Box, ma, 16 * c, y, &full[s]);
+                    tma_load_2d(st + (4 + c) * kF64Box, mb, 16 * c, y, &full[s]);
                 }
             }
         }
@@ -603,83 +606,63 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
     // ---- compute warps
     double *ob = outbox + warp * kF64OutArea;
     for (int k = 0; k < K; ++k) {
-        const int s = k % kF64Stages;
-        f64_wait(&full[s], (unsigned)((k / kF64Stages) & 1));
-        const double *A = base + s * kF64StageBoxes * kF64Box;
-        const double *Bm = A + 4 * kF64Box;
         double acc[16];
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) acc[kk] = 0.0;
         unsigned prev = 0u;
+        for (int p = 0; p < products; ++p) {
+            const int v = k * products + p;
+            const int s = v % kF64Stages;
+            f64_wait(&full[s], (unsigned)((v / kF64Stages) & 1));
+            const double *A = base + s * kF64StageBoxes * kF64Box;
+            const double *Bm = A + 4 * kF64Box;
 #pragma unroll
-        for (int L0 = 0; L0 < 4; ++L0) {
-            const unsigned am = sgn.alpha[L0][warp], bm = sgn.beta[L0][warp];
-            double av[16], bv[16];
-            const double *ab = A + L0 * kF64Box;
-            const double *bb = Bm + (L0 ^ warp) * kF64Box;
+            for (int L0 = 0; L0 < 4; ++L0) {
+                const unsigned am = sgn.alpha[L0][warp], bm = sgn.beta[L0][warp];
+                double av[16], bv[16];
+                const double *ab = A + L0 * kF64Box;
+                const double *bb = Bm + (L0 ^ warp) * kF64Box;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const double2 u = *reinterpret_cast<const double2 *>(&ab[sw128d(lane, j)]);
-                const double2 v = *reinterpret_cast<const double2 *>(&bb[sw128d(lane, j)]);
-                av[2 * j] = u.x; av[2 * j + 1] = u.y;
-                bv[2 * j] = v.x; bv[2 * j + 1] = v.y;
+                for (int j = 0; j < 8; ++j) {
+                    const double2 u = *reinterpret_cast<const double2 *>(&ab[sw128d(lane, j)]);
+                    const double2 v = *reinterpret_cast<const double2 *>(&bb[sw128d(lane, j)]);
+                    av[2 * j] = u.x; av[2 * j + 1] = u.y;
+                    bv[2 * j] = v.x; bv[2 * j + 1] = v.y;
+                }
+#pragma unroll
+                for (int i = 0; i < 16; ++i) av[i] = flip_bit(av[i], (am >> i) & 1u);
+                const unsigned bf = sgn.bflip[L0 ^ warp];
+                if (bf != 0u) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) bv[j] = flip_bit(bv[j], (bf >> j) & 1u);
+                }
+                const unsigned fm = bm ^ prev;
+#pragma unroll
+                for (int kk = 0; kk < 16; ++kk) acc[kk] = flip_bit(acc[kk], (fm >> kk) & 1u);
+                prev = bm;
+                f64_block<NEG>(av, bv, acc, std::make_integer_sequence<int, 256>{});
             }
-#pragma unroll
-            for (int i = 0; i < 16; ++i) av[i] = flip_bit(av[i], (am >> i) & 1u);
-            const unsigned bf = sgn.bflip[L0 ^ warp];
-            if (bf != 0u) {
-#pragma unroll
-                for (int j = 0; j < 16; ++j) bv[j] = flip_bit(bv[j], (bf >> j) & 1u);
-            }
-            const unsigned fm = bm ^ prev;
-#pragma unroll
-            for (int kk = 0; kk < 16; ++kk) acc[kk] = flip_bit(acc[kk], (fm >> kk) & 1u);
-            prev = bm;
-            f64_block<NEG>(av, bv, acc, std::make_integer_sequence<int, 256>{});
+            // The warp is done reading stage s.
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(&empty[s])) : "memory");
         }
-        // The warp is done reading stage s.
-        __syncwarp();
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(&empty[s])) : "memory");
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) acc[kk] = flip_bit(acc[kk], (prev >> kk) & 1u);
         const size_t row0 = (blockIdx.x + (size_t)k * gridDim.x) * kF64Rows;
-        if (acc_out == nullptr) {
-            // The store of tile k - 1 from this warp's box must have finished reading it.
-            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
-            __syncwarp();
+        // The store of tile k - 1 from this warp's box must have finished reading it.
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+        __syncwarp();
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                *reinterpret_cast<double2 *>(&ob[sw128d(lane, j)]) = make_double2(acc[2 * j], acc[2 * j + 1]);
-            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-            __syncwarp();
-            if (lane == 0) {
-                tma_store_2d(&map_out, 16 * warp, (int)row0, ob);
-                asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
-            }
-        } else {
-            // Each lane adds its 16 outputs into its own row: its slot's previous
-            // reduce (tile k - 1, issued by this lane) must have read the slot.
-            asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
-            double *slot = ob + lane * kF64SlotStride;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                *reinterpret_cast<double2 *>(&slot[2 * j]) = make_double2(acc[2 * j], acc[2 * j + 1]);
-            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-            const size_t row = row0 + (size_t)lane;
-            if (row < batch) {
-                asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f64 [%0], [%1], 128;\n" ::"l"(
-                                 acc_out + row * 64 + 16 * warp),
-                             "r"(smem_u32(slot))
-                             : "memory");
-                asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
-            }
+        for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<double2 *>(&ob[sw128d(lane, j)]) = make_double2(acc[2 * j], acc[2 * j + 1]);
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_2d(&map_out, 16 * warp, (int)row0, ob);
+            asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
         }
     }
-    if (acc_out == nullptr) {
-        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
-    } else {
-        asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
-    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
 }
 
 // [rows][64] float64 tensor, [32][16] boxes, 128-byte swizzle, zero fill.
@@ -729,8 +712,9 @@ bool f64_block_signs(const geo::SignPlan &plan, int neg_low, bool rev_a, bool re
 }
 
 template <int NEG>
-cudaError_t launch_f64_tma_neg(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mo,
-                               const F64BlockSigns &signs, size_t batch, double *acc_out, cudaStream_t stream) {
+cudaError_t launch_f64_tma_neg(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &ma2,
+                               const CUtensorMap &mb2, const CUtensorMap &mo, const F64BlockSigns &signs, size_t batch,
+                               int products, cudaStream_t stream) {
     auto kernel = pairwise_f64_n6_tma_kernel<NEG>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kF64Smem);
     if (e != cudaSuccess) return e;
@@ -741,34 +725,47 @@ cudaError_t launch_f64_tma_neg(const CUtensorMap &ma, const CUtensorMap &mb, con
     const size_t tiles = (batch + kF64Rows - 1) / kF64Rows;
     size_t grid = (size_t)geo::device_sm_count() * (size_t)per_sm;
     if (grid > tiles) grid = tiles;
-    kernel<<<(unsigned)grid, kF64Threads, kF64Smem, stream>>>(ma, mb, mo, signs, batch, acc_out);
+    kernel<<<(unsigned)grid, kF64Threads, kF64Smem, stream>>>(ma, mb, ma2, mb2, mo, signs, batch, products);
     return cudaGetLastError();
 }
 
 template <int... NEG>
-cudaError_t launch_f64_tma_dispatch(int neg, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &mo,
-                                    const F64BlockSigns &signs, size_t batch, double *acc_out, cudaStream_t stream,
+cudaError_t launch_f64_tma_dispatch(int neg, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &ma2,
+                                    const CUtensorMap &mb2, const CUtensorMap &mo, const F64BlockSigns &signs,
+                                    size_t batch, int products, cudaStream_t stream,
                                     std::integer_sequence<int, NEG...>) {
     cudaError_t e = cudaErrorInvalidValue;
-    ((neg == NEG ? (e = launch_f64_tma_neg<NEG>(ma, mb, mo, signs, batch, acc_out, stream), true) : false) || ...);
+    ((neg == NEG ? (e = launch_f64_tma_neg<NEG>(ma, mb, ma2, mb2, mo, signs, batch, products, stream), true)
+                 : false) ||
+     ...);
     return e;
 }
 
-// float64 n = 6 forward on the TMA kernel; false when it does not apply
-// (unaligned operands, no tensor-map encoder, sign table that does not factor).
+// float64 n = 6 forward on the TMA kernel, out = left right, or with left2 and
+// right2 given out = left right + left2 right2 in one pass (the JVP); false when
+// it does not apply (unaligned operands, no tensor-map encoder, sign table that
+// does not factor).
 bool launch_pairwise_f64_fast(const geo::SignPlan &plan, const int8_t *signature, const double *left,
                               const double *right, double *out, size_t batch, cudaStream_t stream, cudaError_t *err,
-                              bool rev_left = false, bool rev_right = false, bool accumulate = false) {
+                              bool rev_left = false, bool rev_right = false, const double *left2 = nullptr,
+                              const double *right2 = nullptr) {
+    const bool two = left2 != nullptr && right2 != nullptr;
     if (plan.blades != 64 || ((uintptr_t)left | (uintptr_t)right | (uintptr_t)out) & 15u) return false;
+    if (two && ((uintptr_t)left2 | (uintptr_t)right2) & 15u) return false;
     int neg_low = 0;
     for (int a = 0; a < 4; ++a)
         if (signature[a] < 0) neg_low |= 1 << a;
     F64BlockSigns signs;
     if (!f64_block_signs(plan, neg_low, rev_left, rev_right, &signs)) return false;
-    CUtensorMap ma, mb, mo;
+    CUtensorMap ma, mb, ma2, mb2, mo;
     if (!encode_rows_f64(&ma, left, batch) || !encode_rows_f64(&mb, right, batch) || !encode_rows_f64(&mo, out, batch))
         return false;
-    *err = launch_f64_tma_dispatch(neg_low, ma, mb, mo, signs, batch, accumulate ? out : nullptr, stream,
+    if (two ? (!encode_rows_f64(&ma2, left2, batch) || !encode_rows_f64(&mb2, right2, batch)) : false) return false;
+    if (!two) {
+        ma2 = ma;
+        mb2 = mb;
+    }
+    *err = launch_f64_tma_dispatch(neg_low, ma, mb, ma2, mb2, mo, signs, batch, two ? 2 : 1, stream,
                                    std::make_integer_sequence<int, 16>{});
     return true;
 }
@@ -847,8 +844,8 @@ extern "C" geo_b200_status_t geo_b200_pairwise_gp_jvp_f64(uint8_t dimension, con
                                                           cudaStream_t stream) {
     if (device_left_tangent == nullptr || device_right_tangent == nullptr || device_out_tangent == nullptr)
         return GEO_B200_INVALID_ARGUMENT;
-    // n = 6: two forward products on the TMA kernel, out = a_dot b, then
-    // out += a b_dot (bulk reduce-add, one rounding per element).
+    // n = 6: one pass of the TMA kernel over both products, out = a_dot b + a b_dot
+    // (one accumulator per output across both).
     const geo::SignPlan *plan = dimension == 6 ? geo::cached_sign_plan(6, signature, 0) : nullptr;
     const bool al = ((uintptr_t)device_left | (uintptr_t)device_right | (uintptr_t)device_left_tangent |
                      (uintptr_t)device_right_tangent | (uintptr_t)device_out_tangent) % 16u == 0u;
@@ -856,13 +853,8 @@ extern "C" geo_b200_status_t geo_b200_pairwise_gp_jvp_f64(uint8_t dimension, con
         tensor_map_encoder() != nullptr) {
         cudaError_t e = cudaSuccess;
         if (launch_pairwise_f64_fast(*plan, signature, device_left_tangent, device_right, device_out_tangent, batch,
-                                     stream, &e)) {
-            if (e == cudaSuccess &&
-                !launch_pairwise_f64_fast(*plan, signature, device_left, device_right_tangent, device_out_tangent,
-                                          batch, stream, &e, false, false, true))
-                e = cudaErrorInvalidValue;  // cannot happen: same plan, alignment and sizes as the first launch
+                                     stream, &e, false, false, device_left, device_right_tangent))
             return from_cuda(e);
-        }
     }
     return launch_pairwise<double, kPairJvp>(dimension, signature, device_left, 0, device_right, device_left_tangent,
                                              device_right_tangent, device_out_tangent, nullptr, batch, stream);

@@ -72,7 +72,8 @@ def test_pairwise_f64_n6_tma_path(oracle):
                 assert tol_close(host(lb), want_l, TOL), (sig, which, max_violation(host(lb), want_l, TOL))
             if rb is not None:
                 assert tol_close(host(rb), want_r, TOL), (sig, which, max_violation(host(rb), want_r, TOL))
-        # JVP: a_dot b stored, then a b_dot added row by row (bulk reduce-add); rows past the batch untouched.
+        # JVP: a_dot b + a b_dot in one pass (the ring alternates the two operand pairs of each tile);
+        # rows past the batch untouched.
         ta, tb = splitmix_uniform(740 + k, (B, 64)), splitmix_uniform(750 + k, (B, 64))
         jt = torch.full((B + 40, 64), 7.0, dtype=torch.float64, device="cuda")
         assert L.geo_b200_pairwise_gp_jvp_f64(6, abi.sig_array(sig), ptr(da), ptr(db), ptr(dev(ta)), ptr(dev(tb)),
