@@ -551,15 +551,16 @@ __device__ __forceinline__ void f64_wait(uint64_t *bar, unsigned parity) {
     atomicAdd(&g_pairwise_tma_wait_failures, 1u);
 }
 
-// products = 1: y = a b. products = 2 (the JVP): y = a b + a2 b2 in one pass;
+// PRODUCTS = 1: y = a b. PRODUCTS = 2 (the JVP): y = a b + a2 b2 in one pass;
 // the ring alternates (a, b) and (a2, b2) tiles of the same rows and the
 // compute warps keep one accumulator across both before the single store.
-template <int NEG>
+// (A compile-time count: a run-time one cost the plain product 4%.)
+template <int NEG, int PRODUCTS>
 __global__ void __launch_bounds__(kF64Threads, 2)
 pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                            const __grid_constant__ CUtensorMap map_a2, const __grid_constant__ CUtensorMap map_b2,
-                           const __grid_constant__ CUtensorMap map_out, const F64BlockSigns signs, size_t batch,
-                           int products) {
+                           const __grid_constant__ CUtensorMap map_out, const F64BlockSigns signs, size_t batch) {
+    constexpr int products = PRODUCTS;
     extern __shared__ unsigned char f64_raw[];
     __shared__ __align__(8) uint64_t full[kF64Stages], empty[kF64Stages];
     __shared__ F64BlockSigns sgn;
@@ -610,6 +611,7 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) acc[kk] = 0.0;
         unsigned prev = 0u;
+#pragma unroll 1
         for (int p = 0; p < products; ++p) {
             const int v = k * products + p;
             const int s = v % kF64Stages;
@@ -715,7 +717,7 @@ template <int NEG>
 cudaError_t launch_f64_tma_neg(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &ma2,
                                const CUtensorMap &mb2, const CUtensorMap &mo, const F64BlockSigns &signs, size_t batch,
                                int products, cudaStream_t stream) {
-    auto kernel = pairwise_f64_n6_tma_kernel<NEG>;
+    auto kernel = products == 2 ? pairwise_f64_n6_tma_kernel<NEG, 2> : pairwise_f64_n6_tma_kernel<NEG, 1>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kF64Smem);
     if (e != cudaSuccess) return e;
     int per_sm = 1;
@@ -725,7 +727,7 @@ cudaError_t launch_f64_tma_neg(const CUtensorMap &ma, const CUtensorMap &mb, con
     const size_t tiles = (batch + kF64Rows - 1) / kF64Rows;
     size_t grid = (size_t)geo::device_sm_count() * (size_t)per_sm;
     if (grid > tiles) grid = tiles;
-    kernel<<<(unsigned)grid, kF64Threads, kF64Smem, stream>>>(ma, mb, ma2, mb2, mo, signs, batch, products);
+    kernel<<<(unsigned)grid, kF64Threads, kF64Smem, stream>>>(ma, mb, ma2, mb2, mo, signs, batch);
     return cudaGetLastError();
 }
 
