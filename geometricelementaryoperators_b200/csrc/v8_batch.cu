@@ -133,6 +133,27 @@ __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(c
     __syncwarp();
     const int b0 = lane, b1 = lane + 32;
     const bool l0 = b0 < N, l1 = b1 < N;
+    // Per-lane sign masks of the geometric-product terms, built once: bit l of
+    // gp_sign[0 / 1] is the sign of the forward term (l, l ^ b) for output b =
+    // b0 / b1 (bit l ^ b of neg[l]); bit q of gp_sign[2 / 3] is the sign of the
+    // right-cotangent term e_q e_b (bit b of neg[q]). With the term loops fully
+    // unrolled each sign is a constant-bit extract. Layout [mask][thread]: a
+    // warp's 8-byte loads are conflict-free.
+    __shared__ uint64_t gp_sign[4][kBatchThreads];
+    {
+        uint64_t f0 = 0, f1 = 0, r0 = 0, r1 = 0;
+        for (int l = 0; l < N; ++l) {
+            const uint64_t w = a.neg[l];
+            f0 |= ((w >> ((l ^ b0) & 63)) & 1ull) << l;
+            f1 |= ((w >> ((l ^ b1) & 63)) & 1ull) << l;
+            r0 |= ((w >> (b0 & 63)) & 1ull) << l;
+            r1 |= ((w >> (b1 & 63)) & 1ull) << l;
+        }
+        gp_sign[0][threadIdx.x] = f0;
+        gp_sign[1][threadIdx.x] = f1;
+        gp_sign[2][threadIdx.x] = r0;
+        gp_sign[3][threadIdx.x] = r1;
+    }
 
     for (size_t s = warp; s < a.batch; s += warps) {
         if (*(volatile int *)a.status != 0) break;
@@ -171,13 +192,13 @@ __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(c
                     // reference src/operator_kernel.c:412-447: left-blade-major, zero left coefficients skipped;
                     // left blade l by a broadcast load, right blade l ^ b by a per-lane load (both in L1)
                     double c0 = 0.0, c1 = 0.0;
-#pragma unroll 8
+                    const uint64_t f0 = gp_sign[0][threadIdx.x], f1 = gp_sign[1][threadIdx.x];
+#pragma unroll
                     for (int l = 0; l < N; ++l) {
                         const double lv = L[l];
                         if (lv == 0.0) continue;
-                        const uint64_t negl = a.neg[l];
-                        if (l0) c0 = add(c0, signed_by(mul(lv, R[l ^ b0]), negl, l ^ b0));
-                        if (l1) c1 = add(c1, signed_by(mul(lv, R[l ^ b1]), negl, l ^ b1));
+                        if (l0) c0 = add(c0, signed_by(mul(lv, R[l ^ b0]), f0, l));
+                        if (l1) c1 = add(c1, signed_by(mul(lv, R[l ^ b1]), f1, l));
                     }
                     o0 = c0;
                     o1 = c1;
@@ -276,20 +297,20 @@ __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(c
                     // reference src/operator_kernel.c:494-539; blade q of the operands by broadcast
                     // loads, cotangent blade b ^ q by a per-lane load (all in L1)
                     const uint64_t neg0 = a.neg[b0 & 63], neg1 = a.neg[b1 & 63];
+                    const uint64_t r0 = gp_sign[2][threadIdx.x], r1 = gp_sign[3][threadIdx.x];
                     double la0 = 0.0, la1 = 0.0, ra0 = 0.0, ra1 = 0.0;
-#pragma unroll 8
+#pragma unroll
                     for (int q = 0; q < N; ++q) {
                         const double rq = rvv[q], lq = lvv[q];
-                        const uint64_t negq = a.neg[q];
                         if (l0) {
                             const double cq0 = cot[b0 ^ q];
                             la0 = add(la0, mul(signed_by(cq0, neg0, q), rq));
-                            ra0 = add(ra0, mul(signed_by(cq0, negq, b0), lq));
+                            ra0 = add(ra0, mul(signed_by(cq0, r0, q), lq));
                         }
                         if (l1) {
                             const double cq1 = cot[b1 ^ q];
                             la1 = add(la1, mul(signed_by(cq1, neg1, q), rq));
-                            ra1 = add(ra1, mul(signed_by(cq1, negq, b1), lq));
+                            ra1 = add(ra1, mul(signed_by(cq1, r1, q), lq));
                         }
                     }
                     if (ln->requires_grad) ok = accumulate2(a, lc, la0, la1, 1.0, b0, b1);
