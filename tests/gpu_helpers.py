@@ -7,7 +7,7 @@ import numpy as np
 
 from geometricelementaryoperators_b200 import abi
 
-TOL = 1e-12  # |a-b| <= TOL (1 + |a| + |b|), the north-star float64 bar
+TOL = 1e-12  # |a-b| <= TOL (1 + |a| + |b|): the float64 parity bar
 TOL_F32 = 1e-5
 
 

@@ -2,7 +2,7 @@
 against the CPU oracle, the committed golden vectors, and full-size properties.
 
 Tolerance: float64 results within |a-b| <= 1e-12 (1+|a|+|b|) of the oracle
-(the reference's own CUDA test uses 1e-10,
+(the float64 parity bar; the reference's own CUDA test uses 1e-10,
 tests/test_batch_gp_cuda.cu:35). Routing and signs are bit-exact (test_oracle).
 """
 from __future__ import annotations
