@@ -176,8 +176,8 @@ ALGORITHM_NAMES = {1: "cayley", 2: "representation"}
 KERNEL_NAMES = {1: "tiled_kernel<64, cycle> (Cayley matrix, FP64 FMA)",
                 2: "rep_ws_kernel<16, 4> (warp-specialised D x D representation, FP64 tensor cores)"}
 # DRAM bytes (read + write) per sample of each kernel family, from one ncu
-# capture of the same step on 2^20 samples (profiles/rep_ws_kernel_cl60_train_2p20.md,
-# profiles/tiled_kernel_n6_train_2p20.md); traffic grows with the samples processed.
+# capture of the same step on 2^20 samples (dram__bytes_read.sum +
+# dram__bytes_write.sum of one launch); traffic grows with the samples processed.
 NCU_TRAFFIC_PER_SAMPLE = {1: (1.073777e9 + 6.1568e6) / 2**20, 2: (1.073927e9 + 4.560896e6) / 2**20}
 
 
@@ -204,10 +204,14 @@ class Trainer:
 
 
 # --------------------------------------------------------------------------- reference arm
+REFERENCE_CHUNK = 1024  # samples per call: the reference's fastest regime
+
+
 def _reference_worker(args):
-    """Run the reference CPU path (compiled from its sources) on `chunks` chunks of
-    1024 samples: batch_gp forward -> residual -> batch_gp VJP, the reference's
-    fastest regime. Returns samples processed."""
+    """Run the reference's batched training step (compiled from its sources) on
+    `chunks` chunks of REFERENCE_CHUNK samples: geo_batch_gp_right_mse_sgd_step_f64
+    = forward, residual, 0.5|r|^2, parameter VJP and the SGD update in one call.
+    Returns samples processed."""
     chunks, seed, signature = args
     import numpy as np
 
@@ -215,17 +219,19 @@ def _reference_worker(args):
 
     ref = Reference()
     rng = np.random.default_rng(seed)
-    x = rng.uniform(-1, 1, (1024, 64))
-    t = rng.uniform(-1, 1, (1024, 64))
+    x = rng.uniform(-1, 1, (REFERENCE_CHUNK, 64))
+    t = rng.uniform(-1, 1, (REFERENCE_CHUNK, 64))
     w = rng.normal(0, 0.125, 64)
     done = 0
     for _ in range(chunks):
-        st, y = ref.forward(signature, x, w, False)
-        r = y - t
-        st2, g = ref.vjp(signature, x, r, False)
-        assert st == 0 and st2 == 0
+        st, w, _ = ref.sgd_step(signature, x, t, 1e-9, w, False)
+        assert st == 0
         done += x.shape[0]
     return done
+
+
+REFERENCE_STEP_NOTE = ("the reference's batch path has no Adam (its Adam lives in the per-sample V8 runtime); "
+                       "the O(64) optimizer update per step is negligible beside the O(B) pass")
 
 
 def reference_step(pool, workers, chunks, signature):
@@ -274,11 +280,16 @@ def run_reference_arm(args, world, rank):
             total += done
             elapsed += dt
     value = total / elapsed
-    sample = (f"each step: {workers} processes x {chunks} chunks of 1024 samples of this workload through the "
-              "reference's batch_gp forward and parameter VJP (the Adam update is O(64) per step)")
+    per_step = workers * chunks * REFERENCE_CHUNK
+    sample = (f"each timed step is a bounded sample of this workload: {workers} processes x {chunks} calls of "
+              f"geo_batch_gp_right_mse_sgd_step_f64 on {REFERENCE_CHUNK} samples ({per_step} samples, not the "
+              f"2^{args.batch_log2}-sample step); {REFERENCE_STEP_NOTE}")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * elapsed / args.steps,
+        "ms_per_step_is": f"the time of one timed sample of {per_step} samples, not of a "
+                          f"2^{args.batch_log2}-sample step",
+        "samples_per_timed_step": per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": headline_config(args, world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": workers, "kind": "reference", "sample": sample},
@@ -304,7 +315,8 @@ def cpu_baseline_leg(negative: int) -> dict:
         chunks += 1
     dt = time.perf_counter() - t0
     return {"value": done / dt, "unit": UNIT, "cores": 1, "kind": kind,
-            "sample": f"{chunks} chunks of 1024 samples of the Cl(6,{negative}) shape (forward+VJP), {dt:.1f} s",
+            "sample": f"{chunks} calls of geo_batch_gp_right_mse_sgd_step_f64 on {REFERENCE_CHUNK} samples of the "
+                      f"Cl({6 - negative},{negative}) shape, {dt:.1f} s; {REFERENCE_STEP_NOTE}",
             "reference_benchmarks": reference_benchmarks()}
 
 

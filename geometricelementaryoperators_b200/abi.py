@@ -151,6 +151,8 @@ SIGNATURES: dict[str, tuple] = {
     "geo_b200_pairwise_gp_vjp_f64": (_I, [_U8, _I8P, _P, _P, _P, _P, _P, _SZ, _P]),
     "geo_b200_pairwise_gp_jvp_f64": (_I, [_U8, _I8P, _P, _P, _P, _P, _P, _SZ, _P]),
     "geo_b200_pairwise_gp_f32": (_I, [_U8, _I8P, _P, _I, _P, _P, _SZ, _P]),
+    "geo_b200_pairwise_wait_failures": (_I, [ctypes.POINTER(ctypes.c_uint), _I]),
+    "geo_b200_pairwise_wait_selftest": (_I, [_I, _P, _SZ, ctypes.c_uint32, _P]),
     "geo_b200_sparse_apply_f64": (_I, [ctypes.POINTER(OperatorPlanI32), _P, _P, _SZ, _P]),
     "geo_b200_sparse_apply_parametric_f64": (_I, [ctypes.POINTER(OperatorPlanI32), _P, _P, _P, _SZ, _P]),
     "geo_b200_sparse_apply_vjp_f64": (_I, [ctypes.POINTER(OperatorPlanI32), _P, _P, _SZ, _P]),

@@ -1,6 +1,7 @@
 // noalloc.cu -- geo_b200_parameter_vjp_noalloc_f64: the parameter VJP with its
 // reduction scratch in a fixed array compiled into the library, for callers
 // that cannot allocate device memory (see geo/geo_b200.h for the contract).
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
 
@@ -23,9 +24,30 @@ static __device__ __align__(256) double g_noalloc_records[(size_t)kRecords * geo
 constexpr int kMaxDevices = 64;
 std::mutex g_mutex;
 double *g_records[kMaxDevices] = {};
+CUcontext g_context[kMaxDevices] = {};  // the context the address belongs to
+
+// The current driver context (null when the driver entry point is missing).
+CUcontext current_context() {
+    using Fn = CUresult (*)(CUcontext *);
+    static Fn fn = []() -> Fn {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            (void)cudaGetLastError();
+            return nullptr;
+        }
+        return reinterpret_cast<Fn>(p);
+    }();
+    CUcontext ctx = nullptr;
+    if (fn != nullptr && fn(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    return ctx;
+}
 
 // Device address of the array on the current device (host code cannot use the
-// symbol's name as a pointer). Looked up once per device.
+// symbol's name as a pointer). Looked up once per device, and again only when
+// the device's context is no longer the one the address was taken in (after a
+// cudaDeviceReset the module is loaded anew and the old address is stale).
 geo_b200_status_t records_for_current_device(double **out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
@@ -33,13 +55,15 @@ geo_b200_status_t records_for_current_device(double **out) {
         return GEO_B200_RUNTIME_FAILURE;
     }
     std::lock_guard<std::mutex> lock(g_mutex);
-    if (g_records[dev] == nullptr) {
+    const CUcontext ctx = g_records[dev] != nullptr ? current_context() : nullptr;
+    if (g_records[dev] == nullptr || ctx != g_context[dev]) {
         double *ptr = nullptr;
         if (cudaGetSymbolAddress((void **)&ptr, g_noalloc_records) != cudaSuccess || ptr == nullptr) {
             (void)cudaGetLastError();
             return GEO_B200_RUNTIME_FAILURE;
         }
         g_records[dev] = ptr;
+        g_context[dev] = current_context();
     }
     *out = g_records[dev];
     return GEO_B200_OK;

@@ -248,6 +248,10 @@ constexpr int kTmaStages = 2;
 constexpr int kTmaSub = kTmaRows * 32;  // floats of one [64][32] box (8 KB)
 constexpr uint32_t kTmaWaitLimit = 1u << 22;
 
+// Give-ups of the TMA kernels' bounded waits on this device (read and reset by
+// geo_b200_pairwise_wait_failures). Such a CTA stops issuing loads,
+// waits (bounded) for the loads it has in flight, writes NaN into every output
+// row it had not yet stored and ends.
 __device__ unsigned g_pairwise_tma_wait_failures;
 
 template <bool COMPACT>
@@ -264,6 +268,21 @@ __device__ __forceinline__ int sw128(int row, int chunk) { return row * 32 + ((c
 
 __device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
 
+// Waits for phase `parity` of an mbarrier for at most `limit` polls; false when it gave up.
+__device__ __forceinline__ bool tma_bounded_wait(uint64_t *bar, unsigned parity, uint32_t limit) {
+    const unsigned a = smem_u32(bar);
+    for (uint32_t i = 0; i < limit; ++i) {
+        unsigned done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
@@ -277,10 +296,13 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int x, int 
                  : "memory");
 }
 
-template <int Q, bool COMPACT>
+// STARVE (the wait self-test only): no load is ever issued, so the first wait
+// runs out after `wait_limit` polls with nothing in flight.
+template <int Q, bool COMPACT, bool STARVE = false>
 __global__ void __launch_bounds__(kTmaRows)
 pairwise_f32_n6_tma_kernel(const __grid_constant__ CUtensorMap map_left, const __grid_constant__ CUtensorMap map_right,
-                           const __grid_constant__ CUtensorMap map_out, size_t batch) {
+                           const __grid_constant__ CUtensorMap map_out, float *__restrict__ out, size_t batch,
+                           uint32_t wait_limit) {
     using TT = TmaTile<COMPACT>;
     constexpr int LW = COMPACT ? 32 : 64;
     extern __shared__ unsigned char tma_raw[];
@@ -307,31 +329,19 @@ pairwise_f32_n6_tma_kernel(const __grid_constant__ CUtensorMap map_left, const _
         tma_load_2d(st + TT::A_SUB * kTmaSub, &map_right, 0, y, &bars[s]);
         tma_load_2d(st + (TT::A_SUB + 1) * kTmaSub, &map_right, 32, y, &bars[s]);
     };
-    if (tid == 0)
-        for (int k = 0; k < K && k < kTmaStages; ++k) issue(k);
+    int issued = 0;  // tiles whose loads were issued (thread 0's count)
+    if (tid == 0 && !STARVE)
+        for (; issued < K && issued < kTmaStages; ++issued) issue(issued);
     for (int k = 0; k < K; ++k) {
         const int s = k % kTmaStages;
-        if (tid == 0 && k >= 1 && k + kTmaStages - 1 < K) {
+        if (!STARVE && tid == 0 && k >= 1 && k + kTmaStages - 1 < K) {
             // The stage of tile k + 2 last held tile k - 1, whose store (the
             // latest one) must have finished reading it.
             asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
             issue(k + kTmaStages - 1);
+            issued = k + kTmaStages;
         }
-        {
-            const unsigned a = smem_u32(&bars[s]), parity = (unsigned)((k / kTmaStages) & 1);
-            bool ok = false;
-            for (uint32_t i = 0; i < kTmaWaitLimit && !ok; ++i) {
-                unsigned done;
-                asm volatile(
-                    "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, "
-                    "p;\n}\n"
-                    : "=r"(done)
-                    : "r"(a), "r"(parity)
-                    : "memory");
-                ok = done != 0;
-            }
-            if (!ok) atomicAdd(&g_pairwise_tma_wait_failures, 1u);
-        }
+        const bool ok = tma_bounded_wait(&bars[s], (unsigned)((k / kTmaStages) & 1), wait_limit);
         float *st = base + s * TT::STAGE;
         float *rb = st + TT::A_SUB * kTmaSub;
         float a[LW], b[64], y[64];
@@ -354,7 +364,23 @@ pairwise_f32_n6_tma_kernel(const __grid_constant__ CUtensorMap map_left, const _
             *reinterpret_cast<float4 *>(&rb[(j >> 3) * kTmaSub + sw128(tid, j & 7)]) =
                 make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-        __syncthreads();
+        if (__syncthreads_or(!ok)) {
+            // Some thread's wait gave up: tiles k..K-1 are not stored from the
+            // ring. Wait (bounded) for the loads still in flight, then write
+            // NaN into their rows.
+            if (tid == 0) {
+                for (int j = k; j < issued; ++j)
+                    (void)tma_bounded_wait(&bars[j % kTmaStages], (unsigned)((j / kTmaStages) & 1), wait_limit);
+                asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+                atomicAdd(&g_pairwise_tma_wait_failures, 1u);
+            }
+            for (int j = k; j < K; ++j) {
+                const size_t row = (blockIdx.x + (size_t)j * gridDim.x) * kTmaRows + (size_t)tid;
+                if (row < batch)
+                    for (int c = 0; c < 64; ++c) out[row * 64 + c] = __int_as_float(0x7fc00000);
+            }
+            return;
+        }
         if (tid == 0) {
             const int row = (int)((blockIdx.x + (size_t)k * gridDim.x) * kTmaRows);
             tma_store_2d(&map_out, 0, row, rb);
@@ -393,10 +419,10 @@ bool encode_rows(CUtensorMap *map, const float *ptr, int cols, size_t rows) {
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int Q, bool COMPACT>
-cudaError_t launch_f32_tma(const CUtensorMap &ml, const CUtensorMap &mr, const CUtensorMap &mo, size_t batch,
-                           cudaStream_t stream) {
-    auto kernel = pairwise_f32_n6_tma_kernel<Q, COMPACT>;
+template <int Q, bool COMPACT, bool STARVE = false>
+cudaError_t launch_f32_tma(const CUtensorMap &ml, const CUtensorMap &mr, const CUtensorMap &mo, float *out,
+                           size_t batch, cudaStream_t stream, uint32_t wait_limit = kTmaWaitLimit) {
+    auto kernel = pairwise_f32_n6_tma_kernel<Q, COMPACT, STARVE>;
     const size_t smem = TmaTile<COMPACT>::SMEM;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -407,7 +433,7 @@ cudaError_t launch_f32_tma(const CUtensorMap &ml, const CUtensorMap &mr, const C
     const size_t tiles = (batch + kTmaRows - 1) / kTmaRows;
     size_t grid = (size_t)geo::device_sm_count() * (size_t)per_sm;
     if (grid > tiles) grid = tiles;
-    kernel<<<(unsigned)grid, kTmaRows, smem, stream>>>(ml, mr, mo, batch);
+    kernel<<<(unsigned)grid, kTmaRows, smem, stream>>>(ml, mr, mo, out, batch, wait_limit);
     return cudaGetLastError();
 }
 
@@ -432,8 +458,8 @@ bool launch_pairwise_f32_fast(const int8_t *signature, const float *left, int co
             encode_rows(&mo, out, 64, batch)) {
 #define GEO_F32_TMA_CASE(QQ)                                                                        \
     case QQ:                                                                                        \
-        *err = compact ? launch_f32_tma<QQ, true>(ml, mr, mo, batch, stream)                       \
-                       : launch_f32_tma<QQ, false>(ml, mr, mo, batch, stream);                     \
+        *err = compact ? launch_f32_tma<QQ, true>(ml, mr, mo, out, batch, stream)                  \
+                       : launch_f32_tma<QQ, false>(ml, mr, mo, out, batch, stream);                \
         return true;
             switch (q) {
                 GEO_F32_TMA_CASE(0) GEO_F32_TMA_CASE(1) GEO_F32_TMA_CASE(2) GEO_F32_TMA_CASE(3) GEO_F32_TMA_CASE(4)
@@ -536,34 +562,29 @@ __device__ __forceinline__ double flip_bit(double v, unsigned bit) {
 // Double offset of (row, 16-byte chunk j) in a [32][16] float64 box with the 128-byte swizzle.
 __device__ __forceinline__ int sw128d(int row, int chunk) { return row * 16 + ((chunk ^ (row & 7)) << 1); }
 
-// Bounded wait for phase `parity` of an mbarrier; counts a give-up.
-__device__ __forceinline__ void f64_wait(uint64_t *bar, unsigned parity) {
-    const unsigned a = smem_u32(bar);
-    for (uint32_t i = 0; i < kTmaWaitLimit; ++i) {
-        unsigned done;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(done)
-            : "r"(a), "r"(parity)
-            : "memory");
-        if (done) return;
-    }
-    atomicAdd(&g_pairwise_tma_wait_failures, 1u);
-}
-
 // PRODUCTS = 1: y = a b. PRODUCTS = 2 (the JVP): y = a b + a2 b2 in one pass;
 // the ring alternates (a, b) and (a2, b2) tiles of the same rows and the
 // compute warps keep one accumulator across both before the single store.
 // (A compile-time count: a run-time one cost the plain product 4%.)
-template <int NEG, int PRODUCTS>
+//
+// Every wait is bounded by `wait_limit` polls. A compute warp whose wait gives
+// up (or that finds the CTA aborted) raises the CTA's abort flag, writes NaN
+// into its 16 output columns of every row it has not stored and ends; the
+// producer stops issuing once the flag is up or its own wait gives up, and
+// before it ends waits (bounded) for the loads it issued, so no copy into the
+// CTA's shared memory outlives the CTA. STARVE (the wait self-test only)
+// issues no load at all.
+template <int NEG, int PRODUCTS, bool STARVE = false>
 __global__ void __launch_bounds__(kF64Threads, 2)
 pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                            const __grid_constant__ CUtensorMap map_a2, const __grid_constant__ CUtensorMap map_b2,
-                           const __grid_constant__ CUtensorMap map_out, const F64BlockSigns signs, size_t batch) {
+                           const __grid_constant__ CUtensorMap map_out, const F64BlockSigns signs,
+                           double *__restrict__ out, size_t batch, uint32_t wait_limit) {
     constexpr int products = PRODUCTS;
     extern __shared__ unsigned char f64_raw[];
     __shared__ __align__(8) uint64_t full[kF64Stages], empty[kF64Stages];
     __shared__ F64BlockSigns sgn;
+    __shared__ volatile int s_abort;
     double *base = reinterpret_cast<double *>(((uintptr_t)f64_raw + 1023) & ~(uintptr_t)1023);
     double *outbox = base + kF64Stages * kF64StageBoxes * kF64Box;  // one output area per compute warp
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -577,16 +598,23 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
         }
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         sgn = signs;
+        s_abort = 0;
     }
     __syncthreads();
     if (warp == kF64Compute) {
         // ---- producer: one thread keeps the ring full
-        if (lane == 0) {
+        if (lane == 0 && !STARVE) {
             // stage loads v = 0, 1, ...: tile v / products, operand pair v % products
+            int issued = 0;
             for (int v = 0; v < K * products; ++v) {
                 const int s = v % kF64Stages;
                 // the stage last held load v - kF64Stages: wait until all compute warps released it
-                if (v >= kF64Stages) f64_wait(&empty[s], (unsigned)((v / kF64Stages - 1) & 1));
+                if (v >= kF64Stages &&
+                    !tma_bounded_wait(&empty[s], (unsigned)((v / kF64Stages - 1) & 1), wait_limit)) {
+                    s_abort = 1;
+                    atomicAdd(&g_pairwise_tma_wait_failures, 1u);
+                }
+                if (s_abort) break;
                 double *st = base + s * kF64StageBoxes * kF64Box;
                 const int y = (int)((blockIdx.x + (size_t)(v / products) * gridDim.x) * kF64Rows);
                 const bool second = v % products != 0;
@@ -600,7 +628,12 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
                     tma_load_2d(st + c * kF64Box, ma, 16 * c, y, &full[s]);
                     tma_load_2d(st + (4 + c) * kF64Box, mb, 16 * c, y, &full[s]);
                 }
+                issued = v + 1;
             }
+            // Every load before issued - kF64Stages completed before its stage was
+            // reissued; wait for the last one of each stage.
+            for (int v = issued > kF64Stages ? issued - kF64Stages : 0; v < issued; ++v)
+                (void)tma_bounded_wait(&full[v % kF64Stages], (unsigned)((v / kF64Stages) & 1), wait_limit);
         }
         return;
     }
@@ -611,11 +644,16 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) acc[kk] = 0.0;
         unsigned prev = 0u;
+        bool failed = false;
 #pragma unroll 1
         for (int p = 0; p < products; ++p) {
             const int v = k * products + p;
             const int s = v % kF64Stages;
-            f64_wait(&full[s], (unsigned)((v / kF64Stages) & 1));
+            const bool ok = tma_bounded_wait(&full[s], (unsigned)((v / kF64Stages) & 1), wait_limit);
+            if (__any_sync(0xffffffffu, !ok) || s_abort) {
+                failed = true;
+                break;
+            }
             const double *A = base + s * kF64StageBoxes * kF64Box;
             const double *Bm = A + 4 * kF64Box;
 #pragma unroll
@@ -647,6 +685,20 @@ pairwise_f64_n6_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __gr
             // The warp is done reading stage s.
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(&empty[s])) : "memory");
+        }
+        if (failed) {
+            // Abort: NaN into this warp's columns of tiles k..K-1 (plain stores),
+            // then let this warp's pending tensor stores finish.
+            if (lane == 0) {
+                s_abort = 1;
+                atomicAdd(&g_pairwise_tma_wait_failures, 1u);
+            }
+            for (int j = k; j < K; ++j) {
+                const size_t row = (blockIdx.x + (size_t)j * gridDim.x) * kF64Rows + (size_t)lane;
+                if (row < batch)
+                    for (int c = 0; c < 16; ++c) out[row * 64 + 16 * warp + c] = __longlong_as_double(0x7ff8000000000000ll);
+            }
+            break;
         }
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) acc[kk] = flip_bit(acc[kk], (prev >> kk) & 1u);
@@ -713,11 +765,11 @@ bool f64_block_signs(const geo::SignPlan &plan, int neg_low, bool rev_a, bool re
     return true;
 }
 
-template <int NEG>
+template <int NEG, bool STARVE = false>
 cudaError_t launch_f64_tma_neg(const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &ma2,
-                               const CUtensorMap &mb2, const CUtensorMap &mo, const F64BlockSigns &signs, size_t batch,
-                               int products, cudaStream_t stream) {
-    auto kernel = products == 2 ? pairwise_f64_n6_tma_kernel<NEG, 2> : pairwise_f64_n6_tma_kernel<NEG, 1>;
+                               const CUtensorMap &mb2, const CUtensorMap &mo, const F64BlockSigns &signs, double *out,
+                               size_t batch, int products, cudaStream_t stream, uint32_t wait_limit = kTmaWaitLimit) {
+    auto kernel = products == 2 ? pairwise_f64_n6_tma_kernel<NEG, 2, STARVE> : pairwise_f64_n6_tma_kernel<NEG, 1, STARVE>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kF64Smem);
     if (e != cudaSuccess) return e;
     int per_sm = 1;
@@ -727,17 +779,17 @@ cudaError_t launch_f64_tma_neg(const CUtensorMap &ma, const CUtensorMap &mb, con
     const size_t tiles = (batch + kF64Rows - 1) / kF64Rows;
     size_t grid = (size_t)geo::device_sm_count() * (size_t)per_sm;
     if (grid > tiles) grid = tiles;
-    kernel<<<(unsigned)grid, kF64Threads, kF64Smem, stream>>>(ma, mb, ma2, mb2, mo, signs, batch);
+    kernel<<<(unsigned)grid, kF64Threads, kF64Smem, stream>>>(ma, mb, ma2, mb2, mo, signs, out, batch, wait_limit);
     return cudaGetLastError();
 }
 
 template <int... NEG>
 cudaError_t launch_f64_tma_dispatch(int neg, const CUtensorMap &ma, const CUtensorMap &mb, const CUtensorMap &ma2,
                                     const CUtensorMap &mb2, const CUtensorMap &mo, const F64BlockSigns &signs,
-                                    size_t batch, int products, cudaStream_t stream,
+                                    double *out, size_t batch, int products, cudaStream_t stream,
                                     std::integer_sequence<int, NEG...>) {
     cudaError_t e = cudaErrorInvalidValue;
-    ((neg == NEG ? (e = launch_f64_tma_neg<NEG>(ma, mb, ma2, mb2, mo, signs, batch, products, stream), true)
+    ((neg == NEG ? (e = launch_f64_tma_neg<NEG>(ma, mb, ma2, mb2, mo, signs, out, batch, products, stream), true)
                  : false) ||
      ...);
     return e;
@@ -767,7 +819,7 @@ bool launch_pairwise_f64_fast(const geo::SignPlan &plan, const int8_t *signature
         ma2 = ma;
         mb2 = mb;
     }
-    *err = launch_f64_tma_dispatch(neg_low, ma, mb, ma2, mb2, mo, signs, batch, two ? 2 : 1, stream,
+    *err = launch_f64_tma_dispatch(neg_low, ma, mb, ma2, mb2, mo, signs, out, batch, two ? 2 : 1, stream,
                                    std::make_integer_sequence<int, 16>{});
     return true;
 }
@@ -876,4 +928,44 @@ extern "C" geo_b200_status_t geo_b200_pairwise_gp_f32(uint8_t dimension, const i
     }
     return launch_pairwise<float, kPairForward>(dimension, signature, device_left, left_even_compact != 0,
                                                 device_right, nullptr, nullptr, device_out, nullptr, batch, stream);
+}
+
+extern "C" geo_b200_status_t geo_b200_pairwise_wait_failures(unsigned *count, int reset) {
+    if (count == nullptr) return GEO_B200_INVALID_ARGUMENT;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(count, g_pairwise_tma_wait_failures, sizeof(unsigned));
+    if (e == cudaSuccess && reset) {
+        const unsigned zero = 0;
+        e = cudaMemcpyToSymbol(g_pairwise_tma_wait_failures, &zero, sizeof(unsigned));
+    }
+    if (e != cudaSuccess) return from_cuda(e);
+    return *count != 0 ? GEO_B200_TIMEOUT : GEO_B200_OK;
+}
+
+extern "C" geo_b200_status_t geo_b200_pairwise_wait_selftest(int precision, void *device_out, size_t batch,
+                                                             uint32_t wait_limit, cudaStream_t stream) {
+    if (device_out == nullptr || batch == 0 || wait_limit == 0 || (precision != 32 && precision != 64) ||
+        ((uintptr_t)device_out & 15u) != 0 || tensor_map_encoder() == nullptr)
+        return GEO_B200_INVALID_ARGUMENT;
+    unsigned before = 0;
+    geo_b200_status_t st = geo_b200_pairwise_wait_failures(&before, 1);
+    if (st != GEO_B200_OK && st != GEO_B200_TIMEOUT) return st;
+    cudaError_t e = cudaSuccess;
+    if (precision == 64) {
+        double *out = static_cast<double *>(device_out);
+        CUtensorMap m;
+        if (!encode_rows_f64(&m, out, batch)) return GEO_B200_INVALID_ARGUMENT;
+        F64BlockSigns signs;
+        memset(&signs, 0, sizeof signs);
+        e = launch_f64_tma_neg<0, true>(m, m, m, m, m, signs, out, batch, 1, stream, wait_limit);
+    } else {
+        float *out = static_cast<float *>(device_out);
+        CUtensorMap m;
+        if (!encode_rows(&m, out, 64, batch)) return GEO_B200_INVALID_ARGUMENT;
+        e = launch_f32_tma<0, false, true>(m, m, m, out, batch, stream, wait_limit);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return from_cuda(e);
+    unsigned count = 0;
+    return geo_b200_pairwise_wait_failures(&count, 1);
 }

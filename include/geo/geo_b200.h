@@ -237,8 +237,9 @@ int geo_b200_v8_batch_forward(void *program, uint32_t input_node, const double *
  * batch: batch_size must not exceed GEO_B200_NOALLOC_MAX_BATCH (131072
  * samples, any dimension); larger batches are rejected with
  * GEO_B200_INVALID_ARGUMENT before anything is launched. The first call on each
- * device looks up the array's device address (a one-time set-up per device);
- * make that first call before any stream capture. All calls share the one
+ * device looks up the array's device address (a one-time set-up per device,
+ * repeated only if the device's context was recreated, e.g. after
+ * cudaDeviceReset); make that first call before any stream capture. All calls share the one
  * array and every call overwrites the part it uses, so calls whose kernels
  * overlap on the GPU (different streams without ordering) race; order them on
  * one stream. */
@@ -272,6 +273,24 @@ geo_b200_status_t geo_b200_pairwise_gp_jvp_f64(uint8_t dimension, const int8_t *
 geo_b200_status_t geo_b200_pairwise_gp_f32(uint8_t dimension, const int8_t *signature, const float *device_left,
                                            int left_even_compact, const float *device_right, float *device_out,
                                            size_t batch, cudaStream_t stream);
+
+/* Bounded waits of the n = 6 TMA pairwise kernels (no counterpart in the
+ * reference, whose products run on the CPU). Every wait of those kernels on a
+ * load or on a ring stage gives up after a fixed number of polls; a CTA whose
+ * wait gave up stops loading, waits (bounded) for its loads in flight, writes
+ * NaN into every output row it had not stored and ends, so the context stays
+ * usable. This call synchronizes the current device and reports how many
+ * give-ups (one per CTA of the float32 kernel, one per warp of the float64
+ * kernel) were recorded since the last reset (*count); reset != 0 clears it.
+ * Returns GEO_B200_TIMEOUT when the count is non-zero. */
+geo_b200_status_t geo_b200_pairwise_wait_failures(unsigned *count, int reset);
+/* Self-test of that failure path: runs the float64 (precision 64) or float32
+ * (precision 32) TMA pairwise kernel over `batch` rows of device_out with no
+ * load issued at all, so every first wait runs out after wait_limit polls with
+ * no copy in flight. Synchronizes the stream; returns GEO_B200_TIMEOUT when the
+ * kernel reported its give-up (device_out then holds NaN in every row). */
+geo_b200_status_t geo_b200_pairwise_wait_selftest(int precision, void *device_out, size_t batch,
+                                                  uint32_t wait_limit, cudaStream_t stream);
 
 /* ---- 4. sparse fixed-multivector plans over a batch ------------------- */
 

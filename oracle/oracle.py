@@ -502,7 +502,11 @@ def reference_available() -> bool:
 
 
 def ensure_reference_built() -> bool:
-    """Build oracle/_ref with `make -C oracle ref` when the reference tree is present."""
-    if not REF_SO.exists():
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref"], capture_output=True)
+    """Build oracle/_ref with `make -C oracle ref` when the environment names the
+    reference tree (GEO_REFERENCE_TREE); otherwise report whether it was built."""
+    import os
+
+    tree = os.environ.get("GEO_REFERENCE_TREE")
+    if not REF_SO.exists() and tree:
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={tree}"], capture_output=True)
     return REF_SO.exists()

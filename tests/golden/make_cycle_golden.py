@@ -8,7 +8,7 @@ checkpoints, predictions, exported C headers and its printed PASS lines. The
 tests compare this library's front end (model_ir.py, CPU) and runner
 (geo_cycle_b200, GPU) against these files.
 
-Usage: python tests/golden/make_cycle_golden.py   (needs the reference tree)
+Usage: python tests/golden/make_cycle_golden.py --reference <reference tree>
 """
 from __future__ import annotations
 
@@ -25,8 +25,7 @@ sys.path.insert(0, str(ROOT))
 
 from geometricelementaryoperators_b200.synthetic import splitmix_uniform  # noqa: E402
 
-REF = pathlib.Path("/root/reference")
-COMPILER = REF / "tools" / "geo_model.py"
+REF: pathlib.Path | None = None  # the reference tree, from --reference
 RUNNER = ROOT / "oracle" / "_ref" / "geo_cycle"
 OUT = pathlib.Path(__file__).resolve().parent / "cycle"
 
@@ -174,9 +173,16 @@ def run(cmd: list[str]) -> subprocess.CompletedProcess:
 
 
 def main() -> None:
+    global REF, COMPILER
+    import argparse
+
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--reference", required=True, type=pathlib.Path, help="root of the reference source tree")
+    REF = ap.parse_args().reference.resolve()
+    COMPILER = REF / "tools" / "geo_model.py"
     if not COMPILER.exists():
-        raise SystemExit("the reference tree is needed to make these fixtures")
-    subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "ref"], check=True)
+        raise SystemExit(f"{COMPILER} not found: --reference must name the reference tree")
+    subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "ref", f"REF={REF}"], check=True)
     if OUT.exists():
         shutil.rmtree(OUT)
     (OUT / "invalid").mkdir(parents=True)

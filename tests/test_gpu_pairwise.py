@@ -204,3 +204,41 @@ def test_sparse_plans(oracle):
             pv = [oracle.sparse_apply_parametric_vjp(sig, side, blades, params, x[i], c[i]) for i in range(B)]
             assert tol_close(host(o4), np.stack([u for u, _ in pv]), TOL)
             assert tol_close(host(pc), np.sum(np.stack([v for _, v in pv]), axis=0), TOL)
+
+
+@pytest.mark.parametrize("precision", [64, 32])
+def test_tma_wait_gives_up_with_status(precision, oracle):
+    """A bounded wait of the TMA pairwise kernels that runs out is reported: the
+    self-test launches the kernel with no load issued (nothing in flight), so
+    every CTA's first wait gives up after a few polls; the call returns
+    GEO_B200_TIMEOUT, every output row holds NaN, and the context stays usable
+    (a normal product right after matches the oracle)."""
+    import torch
+
+    L = abi.lib()
+    B = 1000 + 17
+    dtype = torch.float64 if precision == 64 else torch.float32
+    out = torch.zeros((B, 64), dtype=dtype, device="cuda")
+    count = ctypes.c_uint(0)
+    assert L.geo_b200_pairwise_wait_failures(ctypes.byref(count), 1) in (0, 7)
+    st = L.geo_b200_pairwise_wait_selftest(precision, ptr(out), B, 64, stream())
+    assert st == 7, abi.lib().geo_b200_status_string(st)  # GEO_B200_TIMEOUT
+    assert bool(torch.isnan(out).all())
+    assert L.geo_b200_pairwise_wait_failures(ctypes.byref(count), 1) == 0 and count.value == 0
+    sig = canonical_signature(6, 0)
+    a, b = splitmix_uniform(901, (B, 64)), splitmix_uniform(902, (B, 64))
+    s = abi.sig_array(sig)
+    if precision == 64:
+        da, db = dev(a), dev(b)
+        assert L.geo_b200_pairwise_gp_f64(6, s, ptr(da), ptr(db), ptr(out), B, stream()) == 0
+        sync()
+        want = np.stack([oracle.gp(sig, a[i], b[i]) for i in range(B)])
+        assert tol_close(host(out), want, TOL)
+    else:
+        da, db = dev(a.astype(np.float32)), dev(b.astype(np.float32))
+        assert L.geo_b200_pairwise_gp_f32(6, s, ptr(da), 0, ptr(db), ptr(out), B, stream()) == 0
+        sync()
+        want = np.stack([oracle.gp(sig, a[i].astype(np.float32).astype(np.float64),
+                                   b[i].astype(np.float32).astype(np.float64)) for i in range(B)])
+        assert tol_close(host(out).astype(np.float64), want, TOL_F32)
+    assert L.geo_b200_pairwise_wait_failures(ctypes.byref(count), 0) == 0 and count.value == 0

@@ -47,6 +47,38 @@ def test_noalloc_vjp_matches_planned_vjp_twice(n, q, left, batch):
         assert tol_close(host(g_new), host(g_ref), TOL), (call, max_violation(host(g_new), host(g_ref), TOL))
 
 
+@pytest.mark.parametrize("n,q,left", [(6, 0, 0), (4, 1, 1)])
+def test_noalloc_vjp_unaligned_rows_and_oracle(n, q, left, oracle):
+    """Rows that start 8 bytes past a 16-byte boundary take the tiled kernel's
+    8-byte-aligned variant, still with the fixed array; two calls in a row match
+    the ordinary entry point and the CPU oracle."""
+    import torch
+
+    L = abi.lib()
+    sig = canonical_signature(n, q)
+    N = 1 << n
+    batch = 3001
+    plan = CudaPlan(sig)
+    for call in range(2):
+        x = splitmix_uniform(6100 + 10 * n + call, (batch, N))
+        c = splitmix_uniform(6200 + 10 * n + call, (batch, N))
+        bx = torch.zeros(batch * N + 1, dtype=torch.float64, device="cuda")
+        bc = torch.zeros(batch * N + 1, dtype=torch.float64, device="cuda")
+        bx[1:] = torch.from_numpy(x.reshape(-1)).cuda()
+        bc[1:] = torch.from_numpy(c.reshape(-1)).cuda()
+        px, pc = ctypes.c_void_p(bx.data_ptr() + 8), ctypes.c_void_p(bc.data_ptr() + 8)
+        g_new, g_ref = dev(np.full(N, np.nan)), dev(np.full(N, np.nan))
+        assert L.geo_b200_parameter_vjp_noalloc_f64(n, abi.sig_array(sig), left, px, pc, batch, ptr(g_new),
+                                                    stream()) == 0
+        assert L.geo_batch_gp_cuda_parameter_vjp_f64(ctypes.byref(plan.dev), px, pc, batch, left, ptr(g_ref),
+                                                     stream()) == 0
+        sync()
+        assert tol_close(host(g_new), host(g_ref), TOL), (call, max_violation(host(g_new), host(g_ref), TOL))
+        st, want = oracle.vjp(sig, x, c, bool(left))
+        assert st == 0
+        assert tol_close(host(g_new), want, TOL), (call, max_violation(host(g_new), want, TOL))
+
+
 def test_noalloc_vjp_rejects_batches_beyond_capacity():
     L = abi.lib()
     sig = canonical_signature(6, 0)
