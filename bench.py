@@ -204,39 +204,53 @@ class Trainer:
 
 
 # --------------------------------------------------------------------------- reference arm
-REFERENCE_CHUNK = 1024  # samples per call: the reference's fastest regime
+REFERENCE_CHUNKS = (16, 32, 64, 128, 256, 1024)  # samples per call tried by the calibration
 
 
 def _reference_worker(args):
-    """Run the reference's batched training step (compiled from its sources) on
-    `chunks` chunks of REFERENCE_CHUNK samples: geo_batch_gp_right_mse_sgd_step_f64
-    = forward, residual, 0.5|r|^2, parameter VJP and the SGD update in one call.
+    """Run the reference's batched training step (compiled from its sources)
+    `calls` times on `chunk` samples: geo_batch_gp_right_mse_sgd_step_f64 =
+    forward, residual, 0.5|r|^2, parameter VJP and the SGD update in one call.
     Returns samples processed."""
-    chunks, seed, signature = args
+    calls, seed, signature, chunk = args
     import numpy as np
 
     from oracle.oracle import Reference
 
     ref = Reference()
     rng = np.random.default_rng(seed)
-    x = rng.uniform(-1, 1, (REFERENCE_CHUNK, 64))
-    t = rng.uniform(-1, 1, (REFERENCE_CHUNK, 64))
+    x = rng.uniform(-1, 1, (chunk, 64))
+    t = rng.uniform(-1, 1, (chunk, 64))
     w = rng.normal(0, 0.125, 64)
     done = 0
-    for _ in range(chunks):
+    for _ in range(calls):
         st, w, _ = ref.sgd_step(signature, x, t, 1e-9, w, False)
         assert st == 0
         done += x.shape[0]
     return done
 
 
+def reference_chunk(signature) -> int:
+    """The call size at which the reference's step runs fastest on this host
+    (its term-major loops favour short calls that stay in cache)."""
+    best, best_rate = REFERENCE_CHUNKS[0], 0.0
+    for chunk in REFERENCE_CHUNKS:
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 0.25:
+            done += _reference_worker((max(1, 256 // chunk), 5, signature, chunk))
+        rate = done / (time.perf_counter() - t0)
+        if rate > best_rate:
+            best, best_rate = chunk, rate
+    return best
+
+
 REFERENCE_STEP_NOTE = ("the reference's batch path has no Adam (its Adam lives in the per-sample V8 runtime); "
                        "the O(64) optimizer update per step is negligible beside the O(B) pass")
 
 
-def reference_step(pool, workers, chunks, signature):
+def reference_step(pool, workers, chunks, signature, chunk):
     t0 = time.perf_counter()
-    done = sum(pool.map(_reference_worker, [(chunks, 17 + i, signature) for i in range(workers)]))
+    done = sum(pool.map(_reference_worker, [(chunks, 17 + i, signature, chunk) for i in range(workers)]))
     return done, time.perf_counter() - t0
 
 
@@ -265,24 +279,26 @@ def run_reference_arm(args, world, rank):
     import multiprocessing as mp
 
     workers = os.cpu_count() or 1
+    chunk = reference_chunk(sig)
     ctx = mp.get_context("spawn")
-    chunks = 2
+    chunks = max(1, 8192 // chunk)
     with ctx.Pool(workers) as pool:
-        reference_step(pool, workers, 1, sig)  # import + warm
-        # size chunks so one step is ~1 s of work on every core
-        done, dt = reference_step(pool, workers, chunks, sig)
+        reference_step(pool, workers, 1, sig, chunk)  # import + warm
+        # size the calls so one step is ~1 s of work on every core
+        done, dt = reference_step(pool, workers, chunks, sig, chunk)
         chunks = max(1, int(chunks * 1.0 / max(dt, 1e-3)))
         for _ in range(args.warmup):
-            reference_step(pool, workers, chunks, sig)
+            reference_step(pool, workers, chunks, sig, chunk)
         total, elapsed = 0, 0.0
         for _ in range(args.steps):
-            done, dt = reference_step(pool, workers, chunks, sig)
+            done, dt = reference_step(pool, workers, chunks, sig, chunk)
             total += done
             elapsed += dt
     value = total / elapsed
-    per_step = workers * chunks * REFERENCE_CHUNK
+    per_step = workers * chunks * chunk
     sample = (f"each timed step is a bounded sample of this workload: {workers} processes x {chunks} calls of "
-              f"geo_batch_gp_right_mse_sgd_step_f64 on {REFERENCE_CHUNK} samples ({per_step} samples, not the "
+              f"geo_batch_gp_right_mse_sgd_step_f64 on {chunk} samples (the fastest call size of "
+              f"{list(REFERENCE_CHUNKS)} on this host; {per_step} samples, not the "
               f"2^{args.batch_log2}-sample step); {REFERENCE_STEP_NOTE}")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
@@ -309,14 +325,16 @@ def cpu_baseline_leg(negative: int) -> dict:
     else:
         return {"value": None, "unit": UNIT, "cores": 1, "kind": "reference",
                 "sample": "unavailable: oracle/_ref not built"}
-    done, t0, chunks = 0, time.perf_counter(), 0
-    while time.perf_counter() - t0 < 10.0 or chunks < 8:
-        done += worker((1, 99 + chunks, sig))
-        chunks += 1
+    chunk = reference_chunk(sig)
+    done, t0, calls = 0, time.perf_counter(), 0
+    while time.perf_counter() - t0 < 10.0 or calls < 8:
+        done += worker((16, 99 + calls, sig, chunk))
+        calls += 16
     dt = time.perf_counter() - t0
     return {"value": done / dt, "unit": UNIT, "cores": 1, "kind": kind,
-            "sample": f"{chunks} calls of geo_batch_gp_right_mse_sgd_step_f64 on {REFERENCE_CHUNK} samples of the "
-                      f"Cl({6 - negative},{negative}) shape, {dt:.1f} s; {REFERENCE_STEP_NOTE}",
+            "sample": f"{calls} calls of geo_batch_gp_right_mse_sgd_step_f64 on {chunk} samples (the fastest call "
+                      f"size of {list(REFERENCE_CHUNKS)} on this host) of the Cl({6 - negative},{negative}) shape, "
+                      f"{dt:.1f} s; {REFERENCE_STEP_NOTE}",
             "reference_benchmarks": reference_benchmarks()}
 
 

@@ -20,7 +20,7 @@ from tests.gpu_helpers import TOL, CudaPlan, dev, host, make_plan, np_ptr, ptr, 
 
 pytestmark = pytest.mark.gpu
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "batch_gp_golden.npz"
-BATCHES = [1, 3, 16, 64, 256, 1000]
+BATCHES = [1, 3, 16, 64, 256, 1000, 1024]  # 1024: the Cl(2,0) inference shape
 
 
 def _lib():
