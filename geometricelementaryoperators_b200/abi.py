@@ -69,6 +69,13 @@ class OperatorPlanI32(ctypes.Structure):
     ]
 
 
+class MvF64(ctypes.Structure):
+    """geo_operator_mv_f64_t: a dense multivector with its metric."""
+
+    _fields_ = [("dimension", ctypes.c_uint8), ("signature", ctypes.c_int8 * 6),
+                ("coefficients", ctypes.c_double * 64)]
+
+
 class OptimizerConfig(ctypes.Structure):
     _fields_ = [
         ("optimizer", ctypes.c_uint32),
@@ -122,6 +129,17 @@ SIGNATURES: dict[str, tuple] = {
     "geo_operator_plan_fixed_blade_i32": (_I, [ctypes.POINTER(OperatorPlanI32), _U8, _I8P, _I, _U8, ctypes.c_int32]),
     "geo_operator_plan_sparse_i32": (
         _I, [ctypes.POINTER(OperatorPlanI32), _U8, _I8P, _I, ctypes.POINTER(OperatorTermI32), _SZ]),
+    "geo_operator_apply_f64": (_I, [ctypes.POINTER(OperatorPlanI32), ctypes.POINTER(MvF64), ctypes.POINTER(MvF64)]),
+    "geo_operator_apply_parametric_f64": (
+        _I, [ctypes.POINTER(OperatorPlanI32), _P, _SZ, ctypes.POINTER(MvF64), ctypes.POINTER(MvF64)]),
+    "geo_operator_apply_f64_vjp": (
+        _I, [ctypes.POINTER(OperatorPlanI32), ctypes.POINTER(MvF64), ctypes.POINTER(MvF64)]),
+    "geo_operator_apply_parametric_f64_vjp": (
+        _I, [ctypes.POINTER(OperatorPlanI32), _P, _SZ, ctypes.POINTER(MvF64), ctypes.POINTER(MvF64),
+             ctypes.POINTER(MvF64), _P, _SZ]),
+    "geo_operator_gp_f64": (_I, [ctypes.POINTER(MvF64)] * 3),
+    "geo_operator_gp_f64_jvp": (_I, [ctypes.POINTER(MvF64)] * 5),
+    "geo_operator_gp_f64_vjp": (_I, [ctypes.POINTER(MvF64)] * 5),
     # geo/geo_b200.h
     "geo_b200_abi_version": (ctypes.c_uint32, []),
     "geo_b200_status_string": (ctypes.c_char_p, [_I]),

@@ -40,6 +40,11 @@ extern "C" {
 
 #define GEO_B200_ABI_VERSION 0x00010000u
 
+/* Status of the per-multivector geo_operator_*_f64 calls (geo/operator_kernel.h)
+ * when the GPU call itself fails (no device, launch or copy error); the
+ * reference's geo_operator_status_t has no such value. */
+#define GEO_OPERATOR_B200_DEVICE_FAILURE 100
+
 typedef enum {
     GEO_B200_OK = 0,
     GEO_B200_INVALID_ARGUMENT = 1,

@@ -17,11 +17,22 @@
  *   geo_operator_plan_fixed_blade_i32 reference src/operator_kernel.c:137-149
  *   geo_operator_plan_sparse_i32      reference src/operator_kernel.c:151-189
  *
- * The per-multivector arithmetic of the reference (geo_operator_gp_f64, its
- * JVP/VJP, geo_operator_apply_*_f64 and their VJPs) is provided in batched,
- * device-resident form by geo/geo_b200.h (geo_b200_pairwise_*,
+ * Exported here (per-multivector float64 arithmetic, computed on the GPU by
+ * one small launch per call on the caller's current device, bit-identical to
+ * the reference; synchronous, like the reference):
+ *   geo_operator_apply_f64                 reference src/operator_kernel.c:191-220
+ *   geo_operator_apply_parametric_f64      reference src/operator_kernel.c:222-254
+ *   geo_operator_apply_f64_vjp             reference src/operator_kernel.c:256-278
+ *   geo_operator_apply_parametric_f64_vjp  reference src/operator_kernel.c:280-334
+ *   geo_operator_gp_f64                    reference src/operator_kernel.c:412-447
+ *   geo_operator_gp_f64_jvp                reference src/operator_kernel.c:449-492
+ *   geo_operator_gp_f64_vjp                reference src/operator_kernel.c:494-539
+ * Their statuses are the reference's, plus GEO_OPERATOR_B200_DEVICE_FAILURE
+ * (geo/geo_b200.h) when the GPU call itself fails. The batched,
+ * device-resident forms are in geo/geo_b200.h (geo_b200_pairwise_*,
  * geo_b200_sparse_*). The modular and Q-format integer paths of the
- * reference are embedded-only and are not part of this library.
+ * reference (geo_operator_apply_mod_i32, geo_operator_apply_q_i32) are
+ * embedded-only and are not part of this library.
  */
 #ifndef GEO_OPERATOR_KERNEL_H
 #define GEO_OPERATOR_KERNEL_H
@@ -123,6 +134,67 @@ geo_operator_status_t geo_operator_plan_sparse_i32(
     geo_operator_side_t side,
     const geo_operator_term_i32_t *terms,
     size_t term_count
+);
+
+/* output = input * plan (right side) or plan * input (left side). */
+geo_operator_status_t geo_operator_apply_f64(
+    const geo_operator_plan_i32_t *plan,
+    const geo_operator_mv_f64_t *input,
+    geo_operator_mv_f64_t *output
+);
+
+/* As geo_operator_apply_f64 with parameters[i] in place of the plan's integer
+ * coefficient of term i (parameter_count must equal the term count). */
+geo_operator_status_t geo_operator_apply_parametric_f64(
+    const geo_operator_plan_i32_t *plan,
+    const double *parameters,
+    size_t parameter_count,
+    const geo_operator_mv_f64_t *input,
+    geo_operator_mv_f64_t *output
+);
+
+/* input_cotangent = M^T output_cotangent for the plan's operator M. */
+geo_operator_status_t geo_operator_apply_f64_vjp(
+    const geo_operator_plan_i32_t *plan,
+    const geo_operator_mv_f64_t *output_cotangent,
+    geo_operator_mv_f64_t *input_cotangent
+);
+
+/* Cotangents of the input and of every parameter of the parametric apply. */
+geo_operator_status_t geo_operator_apply_parametric_f64_vjp(
+    const geo_operator_plan_i32_t *plan,
+    const double *parameters,
+    size_t parameter_count,
+    const geo_operator_mv_f64_t *input,
+    const geo_operator_mv_f64_t *output_cotangent,
+    geo_operator_mv_f64_t *input_cotangent,
+    double *parameter_cotangents,
+    size_t parameter_cotangent_count
+);
+
+/* output = left * right (dense geometric product; zero left coefficients are skipped). */
+geo_operator_status_t geo_operator_gp_f64(
+    const geo_operator_mv_f64_t *left,
+    const geo_operator_mv_f64_t *right,
+    geo_operator_mv_f64_t *output
+);
+
+/* Forward-mode derivative: output_tangent = left_tangent * right + left * right_tangent. */
+geo_operator_status_t geo_operator_gp_f64_jvp(
+    const geo_operator_mv_f64_t *left,
+    const geo_operator_mv_f64_t *right,
+    const geo_operator_mv_f64_t *left_tangent,
+    const geo_operator_mv_f64_t *right_tangent,
+    geo_operator_mv_f64_t *output_tangent
+);
+
+/* Reverse-mode derivative of the geometric product (the two outputs must differ). */
+geo_operator_status_t geo_operator_gp_f64_vjp(
+    const geo_operator_mv_f64_t *left,
+    const geo_operator_mv_f64_t *right,
+    const geo_operator_mv_f64_t *output_cotangent,
+    geo_operator_mv_f64_t *left_cotangent,
+    geo_operator_mv_f64_t *right_cotangent
 );
 
 #ifdef __cplusplus

@@ -56,6 +56,7 @@ def test_ctypes_layouts_match_reference():
     assert abi.CudaPlan.device_signature.offset == 16
     assert ctypes.sizeof(abi.OperatorPlanI32) == 528
     assert abi.OperatorPlanI32.terms.offset == 16
+    assert ctypes.sizeof(abi.MvF64) == 520 and abi.MvF64.coefficients.offset == 8
 
 
 def _gcc(args, tmp_path):
@@ -90,3 +91,25 @@ def test_c11_consumer_runs(tmp_path):
     res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stderr
     assert "GEO_B200_CONSUMER: PASS" in res.stdout
+
+
+def _operator_consumer(tmp_path):
+    exe = tmp_path / "operator_consumer"
+    lib_dir = str(abi.library_path().parent)
+    orc_dir = str(ROOT / "oracle")
+    _gcc([str(ROOT / "tests" / "c" / "operator_consumer.c"), "-I", orc_dir, "-o", str(exe), "-L", lib_dir,
+          "-lgeo_b200", "-L", orc_dir, "-loracle", f"-Wl,-rpath,{lib_dir}", f"-Wl,-rpath,{orc_dir}", "-lm"],
+         tmp_path)
+    return exe
+
+
+def test_c11_operator_consumer_links(tmp_path):
+    """A C11 caller of every reference per-multivector operator symbol links against libgeo_b200.so."""
+    assert _operator_consumer(tmp_path).exists()
+
+
+@pytest.mark.gpu
+def test_c11_operator_consumer_runs(tmp_path):
+    res = subprocess.run([str(_operator_consumer(tmp_path))], capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stderr
+    assert "GEO_B200_OPERATOR_CONSUMER: PASS" in res.stdout
