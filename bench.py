@@ -49,7 +49,8 @@ def parse():
     p.add_argument("--batch-log2", type=int, default=22, help="per-GPU batch = 2^k (22 is the headline shape)")
     p.add_argument("--negative", type=int, default=0, help="q of Cl(6-q, q); 0 = Cl(6,0)")
     p.add_argument("--no-extras", action="store_true", help="skip e2e, Cl(3,3) and cpu_baseline legs")
-    p.add_argument("--leg", choices=["train", "pairwise-f32", "v8-graph", "forward", "operators"], default="train",
+    p.add_argument("--leg", choices=["train", "pairwise-f32", "v8-graph", "forward", "operators", "reference-gpu"],
+                   default="train",
                    help="pairwise-f32: run only the float32 pairwise sweep (for profiling)")
     p.add_argument("--pairwise-log2", type=int, default=26, help="batch 2^k of the float32 pairwise sweep")
     p.add_argument("--algorithm", choices=["auto", "cayley", "representation"], default="auto",
@@ -669,6 +670,90 @@ def forward_leg(lib, X, q, world) -> dict:
             "kernels": out}
 
 
+REF_CUDA_SO = os.path.join(os.path.dirname(os.path.abspath(__file__)), "oracle", "_ref", "libgeo_ref_cuda.so")
+REF_GPU_ROWS = {"planned_forward": 20, "mse_sgd_step": 20, "hand_forward": 16}  # log2 rows per leg
+
+
+def _reference_cuda():
+    """The reference's own CUDA code (src/batch_gp_cuda.cu, src/hand_cuda_comparator.cu)
+    compiled unmodified for sm_100a into oracle/_ref (a comparator, never part of
+    the product), or None when it was not built."""
+    if not os.path.exists(REF_CUDA_SO):
+        return None
+    from geometricelementaryoperators_b200 import abi
+
+    L = ctypes.CDLL(REF_CUDA_SO)  # RTLD_LOCAL, linked -Bsymbolic: its symbols stay its own
+    for name, (res, argtypes) in abi.SIGNATURES.items():
+        if name.startswith(("geo_batch_gp_cuda_", "geo_hand_cuda_")) and hasattr(L, name):
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, argtypes
+    return L
+
+
+def reference_gpu_leg(lib, world) -> dict:
+    """The reference's own CUDA kernels against this library's entry points of the
+    same names, on the same B200, Cl(6,0), float64, parameter on the right: the
+    planned forward, the MSE-SGD step (forward, residual + loss with atomics, the
+    reference's 64-thread serial parameter VJP, SGD) and the hand-written forward.
+    Each pair runs on the same resident rows; rates are rows per second."""
+    import torch
+
+    from geometricelementaryoperators_b200 import abi
+    from oracle.oracle import Reference
+
+    R = _reference_cuda()
+    if R is None:
+        return {"unavailable": "oracle/_ref/libgeo_ref_cuda.so was not built (the reference sources were not "
+                               "present at build time)"}
+    sig = [1] * 6
+    host_plan = Reference().plan(sig)  # the reference's own plan_init
+    rplan, oplan = abi.CudaPlan(), abi.CudaPlan()
+    hp = ctypes.cast(host_plan, ctypes.POINTER(abi.BatchGpPlan))
+    assert R.geo_batch_gp_cuda_plan_upload(ctypes.byref(rplan), hp) == 0
+    assert lib.geo_batch_gp_cuda_plan_upload(ctypes.byref(oplan), hp) == 0
+    rows = 1 << max(REF_GPU_ROWS.values())
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    X = torch.rand((rows, 64), dtype=torch.float64, device="cuda", generator=gen).mul_(2).sub_(1)
+    T = torch.rand((rows, 64), dtype=torch.float64, device="cuda", generator=gen).mul_(2).sub_(1)
+    w = torch.randn(64, dtype=torch.float64, device="cuda", generator=gen).mul_(0.125)
+    Y, Yr, Res = torch.empty_like(X), torch.empty_like(X), torch.empty_like(X)
+    g, loss = torch.empty(64, dtype=torch.float64, device="cuda"), torch.empty(1, dtype=torch.float64, device="cuda")
+    w_r, w_o = w.clone(), w.clone()
+    sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    out = {"workload": "Cl(6,0), float64, parameter on the right; rows per leg: " +
+                       ", ".join(f"{k} 2^{v}" for k, v in REF_GPU_ROWS.items()),
+           "reference_build": "src/batch_gp_cuda.cu + src/hand_cuda_comparator.cu, unmodified, nvcc -O3 "
+                              "-gencode arch=compute_100a,code=sm_100a (oracle/Makefile)"}
+    for name, log2 in REF_GPU_ROWS.items():
+        n = 1 << log2
+        if name == "planned_forward":
+            ref = lambda: R.geo_batch_gp_cuda_planned_forward_f64(ctypes.byref(rplan), P(X), n, P(w), 0, P(Yr), sp)
+            ours = lambda: lib.geo_batch_gp_cuda_planned_forward_f64(ctypes.byref(oplan), P(X), n, P(w), 0, P(Y), sp)
+        elif name == "hand_forward":
+            ref = lambda: R.geo_hand_cuda_forward_f64(ctypes.byref(rplan), P(X), n, P(w), 0, P(Yr), sp)
+            ours = lambda: lib.geo_hand_cuda_forward_f64(ctypes.byref(oplan), P(X), n, P(w), 0, P(Y), sp)
+        else:
+            ref = lambda: R.geo_batch_gp_cuda_mse_sgd_step_f64(ctypes.byref(rplan), P(X), P(T), n, 1e-9, 0, P(w_r),
+                                                               P(Res), P(g), P(loss), sp)
+            ours = lambda: lib.geo_batch_gp_cuda_mse_sgd_step_f64(ctypes.byref(oplan), P(X), P(T), n, 1e-9, 0,
+                                                                  P(w_o), P(Res), P(g), P(loss), sp)
+        ms_ref = _time_launches(ref, world, reps=2, warm=1)
+        ms_ours = _time_launches(ours, world, reps=10, warm=3)
+        entry = {"rows": n, "reference_ms": ms_ref, "ours_ms": ms_ours, "reference_rows_per_s": n / (ms_ref / 1e3),
+                 "ours_rows_per_s": n / (ms_ours / 1e3), "speedup": ms_ref / ms_ours}
+        if name != "mse_sgd_step":
+            assert ref() == 0 and ours() == 0
+            torch.cuda.synchronize()
+            entry["max_abs_diff"] = float((Y[:n] - Yr[:n]).abs().max())
+        out[name] = entry
+    R.geo_batch_gp_cuda_plan_destroy(ctypes.byref(rplan))
+    lib.geo_batch_gp_cuda_plan_destroy(ctypes.byref(oplan))
+    del X, T, Y, Yr, Res
+    torch.cuda.empty_cache()
+    return out
+
+
 # --------------------------------------------------------------------------- main arm
 def run_b200(args, world, rank, local):
     import numpy as np
@@ -858,6 +943,8 @@ def run_b200(args, world, rank, local):
             line["cl41"] = extras["cl41"]
         if world == 1 and not args.no_extras:
             line["cpu_baseline"] = cpu_baseline_leg(q)
+            # Baseline on the GPU: the reference's own CUDA kernels on this B200.
+            line["reference_gpu_baseline"] = reference_gpu_leg(lib, world)
             line["v8_graph"]["cpu_baseline"] = v8_graph_reference_leg()
         print(json.dumps(line), flush=True)
     tr.destroy()
@@ -893,6 +980,13 @@ def main():
             X.mul_(2).sub_(1)
             res = (forward_leg(abi.lib(), X, args.negative, world) if args.leg == "forward"
                    else operator_legs(abi.lib(), X, world))
+            if rank == 0:
+                print(json.dumps(res), flush=True)
+            return
+        if args.leg == "reference-gpu":
+            from geometricelementaryoperators_b200 import abi
+
+            res = reference_gpu_leg(abi.lib(), world)
             if rank == 0:
                 print(json.dumps(res), flush=True)
             return

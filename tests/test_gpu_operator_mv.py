@@ -64,11 +64,26 @@ def skip_operands(n, seed):
 
 
 def ref_lib():
+    """The reference's CPU code (oracle/_ref), with untyped pointer arguments for
+    the per-multivector calls (this module passes abi.MvF64 structs)."""
     from oracle import oracle as orc
 
     if not orc.REF_SO.exists():
         return None
-    return orc.Reference().lib
+    L = ctypes.CDLL(str(orc.REF_SO))
+    P, SZ = ctypes.c_void_p, ctypes.c_size_t
+    for name, args in (("geo_operator_gp_f64", [P] * 3), ("geo_operator_gp_f64_jvp", [P] * 5),
+                       ("geo_operator_gp_f64_vjp", [P] * 5), ("geo_operator_apply_f64", [P] * 3),
+                       ("geo_operator_apply_parametric_f64", [P, P, SZ, P, P]),
+                       ("geo_operator_apply_f64_vjp", [P] * 3),
+                       ("geo_operator_apply_parametric_f64_vjp", [P, P, SZ, P, P, P, P, SZ])):
+        fn = getattr(L, name)
+        fn.argtypes, fn.restype = args, ctypes.c_int
+    return L
+
+
+def byref(v):
+    return ctypes.addressof(v)
 
 
 def test_products_match_reference_bytes(oracle):
@@ -89,16 +104,14 @@ def test_products_match_reference_bytes(oracle):
         jt, wj = abi.MvF64(), abi.MvF64()
         assert L.geo_operator_gp_f64_jvp(A, C, D, A, jt) == OK
         if R is not None:
-            assert R.geo_operator_gp_f64(ctypes.byref(A), ctypes.byref(Bv), ctypes.byref(want)) == OK
+            assert R.geo_operator_gp_f64(byref(A), byref(Bv), byref(want)) == OK
             assert raw(got) == raw(want), (n, q)
-            assert R.geo_operator_gp_f64(ctypes.byref(mv(sig, sa)), ctypes.byref(mv(sig, sb)),
-                                         ctypes.byref(skip_ref)) == OK
+            ma, mb = mv(sig, sa), mv(sig, sb)
+            assert R.geo_operator_gp_f64(byref(ma), byref(mb), byref(skip_ref)) == OK
             assert raw(skip) == raw(skip_ref), (n, q)
-            assert R.geo_operator_gp_f64_vjp(ctypes.byref(A), ctypes.byref(C), ctypes.byref(D), ctypes.byref(wl),
-                                             ctypes.byref(wr)) == OK
+            assert R.geo_operator_gp_f64_vjp(byref(A), byref(C), byref(D), byref(wl), byref(wr)) == OK
             assert raw(gl) == raw(wl) and raw(gr) == raw(wr), (n, q)
-            assert R.geo_operator_gp_f64_jvp(ctypes.byref(A), ctypes.byref(C), ctypes.byref(D), ctypes.byref(A),
-                                             ctypes.byref(wj)) == OK
+            assert R.geo_operator_gp_f64_jvp(byref(A), byref(C), byref(D), byref(A), byref(wj)) == OK
             assert raw(jt) == raw(wj), (n, q)
         else:
             assert np.array_equal(np.array(got.coefficients[:N]), oracle.gp(sig, a, b), equal_nan=True)
@@ -149,15 +162,14 @@ def test_apply_family_matches_reference_bytes(oracle):
                 if R is not None:
                     ref = {k: abi.MvF64() for k in outs}
                     rpc = np.zeros(count)
-                    pb = ctypes.byref(plan)
-                    assert R.geo_operator_apply_f64(pb, ctypes.byref(X), ctypes.byref(ref["apply"])) == OK
-                    assert R.geo_operator_apply_parametric_f64(pb, pp.ctypes.data_as(ctypes.c_void_p), count,
-                                                               ctypes.byref(X), ctypes.byref(ref["param"])) == OK
-                    assert R.geo_operator_apply_f64_vjp(pb, ctypes.byref(Cv), ctypes.byref(ref["vjp"])) == OK
-                    assert R.geo_operator_apply_parametric_f64_vjp(
-                        pb, pv.ctypes.data_as(ctypes.c_void_p), count, ctypes.byref(xf),
-                        ctypes.byref(mv(sig, splitmix_uniform(78 + n, (N,)))), ctypes.byref(ref["pvjp"]),
-                        rpc.ctypes.data_as(ctypes.c_void_p), count) == OK
+                    pb = byref(plan)
+                    cf = mv(sig, splitmix_uniform(78 + n, (N,)))
+                    assert R.geo_operator_apply_f64(pb, byref(X), byref(ref["apply"])) == OK
+                    assert R.geo_operator_apply_parametric_f64(pb, pp.ctypes.data, count, byref(X),
+                                                               byref(ref["param"])) == OK
+                    assert R.geo_operator_apply_f64_vjp(pb, byref(Cv), byref(ref["vjp"])) == OK
+                    assert R.geo_operator_apply_parametric_f64_vjp(pb, pv.ctypes.data, count, byref(xf), byref(cf),
+                                                                   byref(ref["pvjp"]), rpc.ctypes.data, count) == OK
                     for k in outs:
                         assert raw(outs[k]) == raw(ref[k]), (n, q, side, count, k)
                     assert rpc.tobytes() == pc.tobytes()
