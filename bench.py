@@ -671,7 +671,7 @@ def forward_leg(lib, X, q, world) -> dict:
 
 
 REF_CUDA_SO = os.path.join(os.path.dirname(os.path.abspath(__file__)), "oracle", "_ref", "libgeo_ref_cuda.so")
-REF_GPU_ROWS = {"planned_forward": 20, "mse_sgd_step": 20, "hand_forward": 16}  # log2 rows per leg
+REF_GPU_ROWS = {"planned_forward": 20, "mse_sgd_step": 18, "hand_forward": 16}  # log2 rows per leg
 
 
 def _reference_cuda():

@@ -764,6 +764,9 @@ extern "C" int geo_b200_cycle_main(int argc, char **argv) {
         printf("geo_cycle %s GEO_V8_ABI=0x%08x\n", GEO_CYCLE_VERSION, geo_v8_abi_version());
         return EXIT_SUCCESS;
     }
+    // The model compiler (JSON document -> model IR), beside the runner's commands.
+    if (cmd == "compile" && argc == 4) return geo_b200_model_compile(argv[2], argv[3]) ? EXIT_SUCCESS : EXIT_FAILURE;
+    if (cmd == "validate" && argc == 3) return geo_b200_model_compile(argv[2], nullptr) ? EXIT_SUCCESS : EXIT_FAILURE;
     geo_b200_cycle_model_t *m = nullptr;
     int success = 0;
     if (cmd == "check" && argc == 3) {

@@ -19,6 +19,8 @@
 #ifndef GEO_CYCLE_B200_H
 #define GEO_CYCLE_B200_H
 
+#include <stddef.h>
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -49,8 +51,30 @@ int geo_b200_cycle_save_checkpoint(const geo_b200_cycle_model_t *model, const ch
 int geo_b200_cycle_load_checkpoint(geo_b200_cycle_model_t *model, const char *path);
 
 /* The command line of the reference tool (check | train | predict | export-c |
- * --version); returns the process exit status. */
+ * --version), plus the model compiler's two commands (compile <model.json>
+ * <model.geoir> | validate <model.json>); returns the process exit status. */
 int geo_b200_cycle_main(int argc, char **argv);
+
+/* ---- model compiler: JSON model documents -> model IR ------------------------
+ * Replaces the reference's tools/geo_model.py (compile / validate): the same
+ * accepted documents, rules, rule order and messages, the same IR bytes
+ * (including the Mersenne-Twister stream of `random:` initialisers). */
+
+/* Compiles the UTF-8 text of a model document. On success returns 1, sets
+ * *ir_text (may be NULL to validate only) to the NUL-terminated IR text
+ * (release it with geo_b200_model_free_text) and writes the summary
+ * "nodes=.. parameters=.. inputs=.. targets=.. states=.. blade_count=..
+ * batch_size=.." into `summary`; on rejection returns 0 and writes the
+ * reference compiler's message into `error`. */
+int geo_b200_model_compile_text(const char *json_text, size_t json_length, char **ir_text, char *summary,
+                                size_t summary_capacity, char *error, size_t error_capacity);
+void geo_b200_model_free_text(char *text);
+
+/* Reads model_path, compiles it and writes ir_path atomically (temporary file,
+ * fsync, rename), printing "GEO_MODEL_COMPILE: PASS output=<ir_path> <summary>";
+ * with ir_path NULL only validates ("GEO_MODEL_VALIDATE: PASS <summary>").
+ * Rejections print "geo_model: <message>" on stderr and return 0. */
+int geo_b200_model_compile(const char *model_path, const char *ir_path);
 
 #ifdef __cplusplus
 }
