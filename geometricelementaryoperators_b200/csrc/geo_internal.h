@@ -164,6 +164,12 @@ struct RepDevice {
     int32_t blades, D, S, side;
     int32_t raw_stride;  // row stride (doubles) of the staged raw tiles (= blades, unpadded)
     int32_t ws_ready;    // butterfly tables present (warp-specialised kernel usable)
+    // D = 16, S = 4: the signed Pauli string J = P(x = 12, z = 4) (J^2 = -1)
+    // commutes with every rho(e_A). J is then a complex structure on the D
+    // columns (pairs m, m ^ 12, m < 8, sign -1 for m >= 4) that every W' and
+    // every rho(e_A) respects, so the GEMMs are 8 x 8 complex products and the
+    // warp-specialised kernel runs them as three real products each (3M).
+    int32_t cplx;
 };
 bool make_rep_device(RepDevice *out, const RepPlan &plan);
 // True when a tensor-core kernel exists for the plan's (D, S).

@@ -586,7 +586,22 @@ __device__ __forceinline__ void ws_write_record(const RepDevice &rep, const GAcc
 // VJP = false: training pass (x, targets t, parameter W). VJP = true: parameter
 // VJP of given output cotangents c (in place of t, no W): the producers write
 // C' = P c instead of -T', and GEMM 1 is skipped (R' := C').
-template <int D, int S, bool VJP>
+//
+// CPLX (D = 16, S = 4, RepDevice::cplx): the consumers use the complex
+// structure J = P(12, 4). Column pair (m, m ^ 12), m < 8, of a row r of X' is
+// the complex number u - i v with u = r[m], v = s_m r[m ^ 12] (s_m = -1 for
+// m >= 4), and W' is the 8 x 8 complex matrix alpha + i beta with
+// alpha[m][m'] = W'[m][m'], beta[m][m'] = s_m W'[m ^ 12][m']. GEMM 1 is then
+// three real 8 x 8 products per row (Gauss's three-multiplication form):
+//   K1 = (u - v) alpha,  K2 = u (beta - alpha),  K3 = v (alpha + beta),
+//   R'[m'] = K1 + K3 - T'[m'],  R'[m' ^ 12] s_m' = -(K1 + K2) - s_m' T'[m' ^ 12],
+// and GEMM 2 keeps only the complex-linear part of G' = X'^T R', which is all
+// that <G', rho(e_A)> sees (rho(e_A) commutes with J): with p, q the pair of
+// R' entries, P = sum u p + v q and Q = sum v p - u q are
+//   M1 = (u + v) p,  M2 = u (p + q),  M3 = v (p - q),  P = M1 - M3,  Q = M1 - M2.
+// 1536 instead of 2048 FP64 multiply-adds per sample (m8n8k4 tiles), for 192
+// extra additions; the shared-memory access sets are the plain consumer's.
+template <int D, int S, bool VJP, bool CPLX = false>
 __global__ void __launch_bounds__(kWsThreads, 2)
 rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ T,
               const double *__restrict__ W, size_t batch, double *__restrict__ records) {
@@ -625,6 +640,11 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
     // Consumer state (also declared, unused, in the producer warps).
     constexpr int PT = D / 8;  // 8-column tiles of G'
     double gacc[PT][2][D == 16 ? 4 : 2];
+    double c3[3][2][2];  // CPLX: M1, M2, M3 per k slice parity h, the m8n8k4 C fragment
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) c3[a][h][0] = c3[a][h][1] = 0.0;
 #pragma unroll
     for (int p = 0; p < PT; ++p)
 #pragma unroll
@@ -705,6 +725,81 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
                 }
             }
             named_arrive(kBarFull + st, kWsThreads);
+        }
+    } else if constexpr (CPLX) {
+        // ------------------------------------------------------ consumers (3M)
+        static_assert(D == 16 && S == 4, "complex form of the n = 6 quaternionic algebras");
+        const int cw = warp - kWsProducers / 32;
+        const int g = lane >> 2, t4 = lane & 3;
+        constexpr unsigned NEG = 0x80000000u;
+        const unsigned sg_neg = (g & 4) ? NEG : 0u;  // s_g of complex column g
+        // GEMM 1 A fragments (m8n8k4, A[m'][m], m' = g, m = t4 + 4 kk; s_m = -1 for kk = 1).
+        double wk1[2], wk2[2], wk3[2];
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const int m = t4 + 4 * kk;
+            const double al = VJP ? 0.0 : Wp[m * 16 + g];
+            const double be = VJP ? 0.0 : flip_sign(Wp[(m ^ 12) * 16 + g], kk ? NEG : 0u);
+            wk1[kk] = al;
+            wk2[kk] = be - al;
+            wk3[kk] = al + be;
+        }
+        for (int k = 0; k < K; ++k) {
+            const int st = k % kWsStages;
+            named_sync(kBarFull + st, kWsThreads);
+            const double *xs = stages + st * G::STAGE;
+            const double *ts = xs + G::TILE;
+#pragma unroll
+            for (int j = 0; j < G::GPW; ++j) {
+                const int n0 = (cw * G::GPW + j) * 8;
+                double r0[2], r1[2];  // R' pair (p, q) at row n0 + 2 t4 + h, complex column g
+                if constexpr (!VJP) {
+                    // GEMM 1 transposed: K[m' = g][row n0 + 2 t4 + h]; K3 starts at -T'[.][g]
+                    // (stored negated), K2 at +s_g T'[.][g ^ 12].
+                    double k1[2] = {0.0, 0.0}, k2[2], k3[2];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int row = n0 + 2 * t4 + h;
+                        k3[h] = ts[ws_index<16>(row, g)];
+                        k2[h] = flip_sign(ts[ws_index<16>(row, g ^ 12)], sg_neg ^ NEG);
+                    }
+#pragma unroll
+                    for (int kk = 0; kk < 2; ++kk) {
+                        const int m = t4 + 4 * kk;
+                        const double u = xs[ws_index<16>(n0 + g, m)];
+                        const double v = flip_sign(xs[ws_index<16>(n0 + g, m ^ 12)], kk ? NEG : 0u);
+                        mma_8x8x4(k1, wk1[kk], u - v);
+                        mma_8x8x4(k2, wk2[kk], u);
+                        mma_8x8x4(k3, wk3[kk], v);
+                    }
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        r0[h] = k1[h] + k3[h];
+                        r1[h] = -(k1[h] + k2[h]);
+                    }
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int row = n0 + 2 * t4 + h;
+                        r0[h] = ts[ws_index<16>(row, g)];
+                        r1[h] = flip_sign(ts[ws_index<16>(row, g ^ 12)], sg_neg);
+                    }
+                }
+                // GEMM 2: k slot t4 of slice h is row n0 + 2 t4 + h.
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    sq = fma(r0[h], r0[h], sq);
+                    sq = fma(r1[h], r1[h], sq);
+                    worst_exp = max(worst_exp, max(exponent_bits(r0[h]), exponent_bits(r1[h])));
+                    const int row = n0 + 2 * t4 + h;
+                    const double u = xs[ws_index<16>(row, g)];
+                    const double v = flip_sign(xs[ws_index<16>(row, g ^ 12)], sg_neg);
+                    mma_8x8x4(c3[0][h], u + v, r0[h]);
+                    mma_8x8x4(c3[1][h], u, r0[h] + r1[h]);
+                    mma_8x8x4(c3[2][h], v, r0[h] - r1[h]);
+                }
+            }
+            if (k + kWsStages < K) named_arrive(kBarEmpty + st, kWsThreads);
         }
     } else {
         // ------------------------------------------------------------ consumers
@@ -797,7 +892,26 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
     double *Gsum = Gs + 4 * D * D;       // D * D
     double *red = Gsum + D * D;          // kWsThreads
     static_assert(5 * D * D + kWsThreads <= kWsStages * G::STAGE, "epilogue scratch fits");
-    if (warp >= kWsProducers / 32) {
+    if (CPLX && warp >= kWsProducers / 32) {
+        // The complex-linear part of G' in the original columns: entry (m, m')
+        // carries P / 2, (m, m' ^ 12) -s_m' Q / 2, (m ^ 12, m') s_m Q / 2 and
+        // (m ^ 12, m' ^ 12) s_m s_m' P / 2 (halving is exact).
+        const int cw = warp - kWsProducers / 32;
+        const int g = lane >> 2, t4 = lane & 3;
+        double *gw = Gs + cw * D * D;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int m = g, mp = 2 * t4 + i;
+            const double m1 = c3[0][0][i] + c3[0][1][i], m2 = c3[1][0][i] + c3[1][1][i];
+            const double m3 = c3[2][0][i] + c3[2][1][i];
+            const double P = 0.5 * (m1 - m3), Q = 0.5 * (m1 - m2);
+            const unsigned sm = (m & 4) ? 0x80000000u : 0u, sp = (mp & 4) ? 0x80000000u : 0u;
+            gw[m * D + mp] = P;
+            gw[m * D + (mp ^ 12)] = flip_sign(Q, sp ^ 0x80000000u);
+            gw[(m ^ 12) * D + mp] = flip_sign(Q, sm);
+            gw[(m ^ 12) * D + (mp ^ 12)] = flip_sign(P, sm ^ sp);
+        }
+    } else if (warp >= kWsProducers / 32) {
         const int cw = warp - kWsProducers / 32;
         const int g = lane >> 2, t4 = lane & 3;
         double *gw = Gs + cw * D * D;
@@ -845,6 +959,8 @@ cudaError_t launch_rep_ws(const RepDevice &rep, const double *X, const double *T
     using G = WsGeo<D, S>;
     if (rep.raw_stride != G::N || rep.D != D || rep.S != S) return cudaErrorInvalidValue;
     auto kernel = rep_ws_kernel<D, S, VJP>;
+    if constexpr (D == 16 && S == 4)
+        if (rep.cplx) kernel = rep_ws_kernel<16, 4, VJP, true>;
     const size_t smem = (size_t)(D * D + kWsStages * G::STAGE) * sizeof(double) + kWsStages * sizeof(uint64_t);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;

@@ -384,6 +384,12 @@ bool make_rep_device(RepDevice *out, const RepPlan &p) {
     // Warp-specialised kernel: butterfly tables (the kernel exists for
     // D = 16, S >= 2 and D = 8, S >= 4; without tables the synchronous kernel runs).
     if ((D == 16 && S >= 2) || (D == 8 && S >= 4)) out->ws_ready = make_ws_tables(out, p, members) ? 1 : 0;
+    // Complex structure J = P(12, 4): it commutes with P(x_A, z_A) when
+    // popc(z_J & x_A) + popc(z_A & x_J) is even, for every blade A.
+    bool commutes = D == 16 && S == 4;
+    for (int A = 0; commutes && A < N; ++A)
+        commutes = ((__builtin_popcount(4u & p.xm[A]) + __builtin_popcount(12u & p.zm[A])) & 1) == 0;
+    out->cplx = commutes ? 1 : 0;
     return true;
 }
 

@@ -76,6 +76,26 @@ static const char *check_ws_layout(const RepDevice &dev) {
                         }
                         if (!distinct_banks(a)) return "epilogue / GEMM 2 operand conflicts";
                     }
+                // The complex (3M) consumer of D = 16: GEMM 1 reads columns m = t + 4 kk and
+                // m ^ 12 of row n0 + g; T' and GEMM 2 read columns g and g ^ 12 of rows n0 + 2 t + hh.
+                for (int kk = 0; D == 16 && kk < 2; ++kk)
+                    for (int pair = 0; pair < 2; ++pair) {
+                        int a[16];
+                        for (int l = 0; l < 16; ++l) {
+                            const int lane = 16 * h + l, g = lane >> 2, t = lane & 3;
+                            a[l] = ws_index<D>(n0 + g, (t + 4 * kk) ^ (pair ? 12 : 0));
+                        }
+                        if (!distinct_banks(a)) return "3M GEMM 1 operand conflicts";
+                    }
+                for (int hh = 0; D == 16 && hh < 2; ++hh)
+                    for (int pair = 0; pair < 2; ++pair) {
+                        int a[16];
+                        for (int l = 0; l < 16; ++l) {
+                            const int lane = 16 * h + l, g = lane >> 2, t = lane & 3;
+                            a[l] = ws_index<D>(n0 + 2 * t + hh, g ^ (pair ? 12 : 0));
+                        }
+                        if (!distinct_banks(a)) return "3M T' / GEMM 2 operand conflicts";
+                    }
             }
         }
     // rep_fwd_kernel: the consumers' Y' writes (the epilogue positions above)
