@@ -531,16 +531,36 @@ using GAcc = double[D / 8][2][D == 16 ? 4 : 2];
 // rep_ws_kernel carries the same reduction, W' build and group tables inline:
 // moving them onto these helpers changes that kernel's register allocation,
 // and its timing is the measured one.
-template <int D, int S>
-__device__ __forceinline__ void ws_write_record(const RepDevice &rep, const GAcc<D> &gacc, double sq,
-                                                unsigned worst_exp, const unsigned *gave_up, double *scratch,
-                                                double *records) {
+// Consumer partials of the complex (3M) GEMM 2 written as the complex-linear
+// part of G' in the original columns (see rep_ws_kernel's CPLX notes).
+__device__ __forceinline__ void ws_store_complex_partials(const double (&c3)[3][2][2], double *gw) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int m = g, mp = 2 * t4 + i;
+        const double m1 = c3[0][0][i] + c3[0][1][i], m2 = c3[1][0][i] + c3[1][1][i];
+        const double m3 = c3[2][0][i] + c3[2][1][i];
+        const double P = 0.5 * (m1 - m3), Q = 0.5 * (m1 - m2);
+        const unsigned sm = (m & 4) ? 0x80000000u : 0u, sp = (mp & 4) ? 0x80000000u : 0u;
+        gw[m * 16 + mp] = P;
+        gw[m * 16 + (mp ^ 12)] = flip_sign(Q, sp ^ 0x80000000u);
+        gw[(m ^ 12) * 16 + mp] = flip_sign(Q, sm);
+        gw[(m ^ 12) * 16 + (mp ^ 12)] = flip_sign(P, sm ^ sp);
+    }
+}
+
+template <int D, int S, bool CPLX = false>
+__device__ __forceinline__ void ws_write_record(const RepDevice &rep, const GAcc<D> &gacc, const double (&c3)[3][2][2],
+                                                double sq, unsigned worst_exp, const unsigned *gave_up,
+                                                double *scratch, double *records) {
     constexpr int N = D * S, PT = D / 8;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     double *Gs = scratch;                // 4 * D * D
     double *Gsum = Gs + 4 * D * D;       // D * D
     double *red = Gsum + D * D;          // kWsThreads
-    if (warp >= kWsProducers / 32) {
+    if (CPLX && warp >= kWsProducers / 32) {
+        ws_store_complex_partials(c3, Gs + (warp - kWsProducers / 32) * D * D);
+    } else if (warp >= kWsProducers / 32) {
         const int cw = warp - kWsProducers / 32;
         const int g = lane >> 2, t4 = lane & 3;
         double *gw = Gs + cw * D * D;
@@ -728,7 +748,13 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
         }
     } else if constexpr (CPLX) {
         // ------------------------------------------------------ consumers (3M)
+        // Software-pipelined: iteration k loads every operand of tile k from its
+        // stage (GEMM 1 operands, T', GEMM 2's X' operands), issues GEMM 2 of tile
+        // k - 1 from registers and GEMM 1 of tile k (independent streams), and
+        // releases the stage. The accumulation order of GEMM 2 is tile by tile as
+        // without the pipelining.
         static_assert(D == 16 && S == 4, "complex form of the n = 6 quaternionic algebras");
+        constexpr int GP = G::GPW;
         const int cw = warp - kWsProducers / 32;
         const int g = lane >> 2, t4 = lane & 3;
         constexpr unsigned NEG = 0x80000000u;
@@ -744,63 +770,74 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
             wk2[kk] = be - al;
             wk3[kk] = al + be;
         }
+        // GEMM 2 operands of the previous tile: R' pair (p, q) and X' pair (u, v) at
+        // row n0 + 2 t4 + h, complex column g.
+        double pp[GP][2], pq[GP][2], pu[GP][2], pv[GP][2];
+        auto gemm2 = [&]() {
+#pragma unroll
+            for (int j = 0; j < GP; ++j)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    mma_8x8x4(c3[0][h], pu[j][h] + pv[j][h], pp[j][h]);
+                    mma_8x8x4(c3[1][h], pu[j][h], pp[j][h] + pq[j][h]);
+                    mma_8x8x4(c3[2][h], pv[j][h], pp[j][h] - pq[j][h]);
+                }
+        };
         for (int k = 0; k < K; ++k) {
             const int st = k % kWsStages;
             named_sync(kBarFull + st, kWsThreads);
             const double *xs = stages + st * G::STAGE;
             const double *ts = xs + G::TILE;
+            double cu[GP][2], cv[GP][2], k1[GP][2], k2[GP][2], k3[GP][2], bu[GP][2], bv[GP][2];
 #pragma unroll
-            for (int j = 0; j < G::GPW; ++j) {
-                const int n0 = (cw * G::GPW + j) * 8;
-                double r0[2], r1[2];  // R' pair (p, q) at row n0 + 2 t4 + h, complex column g
-                if constexpr (!VJP) {
-                    // GEMM 1 transposed: K[m' = g][row n0 + 2 t4 + h]; K3 starts at -T'[.][g]
-                    // (stored negated), K2 at +s_g T'[.][g ^ 12].
-                    double k1[2] = {0.0, 0.0}, k2[2], k3[2];
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int row = n0 + 2 * t4 + h;
-                        k3[h] = ts[ws_index<16>(row, g)];
-                        k2[h] = flip_sign(ts[ws_index<16>(row, g ^ 12)], sg_neg ^ NEG);
-                    }
-#pragma unroll
-                    for (int kk = 0; kk < 2; ++kk) {
-                        const int m = t4 + 4 * kk;
-                        const double u = xs[ws_index<16>(n0 + g, m)];
-                        const double v = flip_sign(xs[ws_index<16>(n0 + g, m ^ 12)], kk ? NEG : 0u);
-                        mma_8x8x4(k1, wk1[kk], u - v);
-                        mma_8x8x4(k2, wk2[kk], u);
-                        mma_8x8x4(k3, wk3[kk], v);
-                    }
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        r0[h] = k1[h] + k3[h];
-                        r1[h] = -(k1[h] + k2[h]);
-                    }
-                } else {
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int row = n0 + 2 * t4 + h;
-                        r0[h] = ts[ws_index<16>(row, g)];
-                        r1[h] = flip_sign(ts[ws_index<16>(row, g ^ 12)], sg_neg);
-                    }
-                }
-                // GEMM 2: k slot t4 of slice h is row n0 + 2 t4 + h.
+            for (int j = 0; j < GP; ++j) {
+                const int n0 = (cw * GP + j) * 8;
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    sq = fma(r0[h], r0[h], sq);
-                    sq = fma(r1[h], r1[h], sq);
-                    worst_exp = max(worst_exp, max(exponent_bits(r0[h]), exponent_bits(r1[h])));
                     const int row = n0 + 2 * t4 + h;
-                    const double u = xs[ws_index<16>(row, g)];
-                    const double v = flip_sign(xs[ws_index<16>(row, g ^ 12)], sg_neg);
-                    mma_8x8x4(c3[0][h], u + v, r0[h]);
-                    mma_8x8x4(c3[1][h], u, r0[h] + r1[h]);
-                    mma_8x8x4(c3[2][h], v, r0[h] - r1[h]);
+                    cu[j][h] = xs[ws_index<16>(row, g)];
+                    cv[j][h] = flip_sign(xs[ws_index<16>(row, g ^ 12)], sg_neg);
+                    // K3 starts at -T'[.][g] (stored negated), K2 at +s_g T'[.][g ^ 12]; in
+                    // VJP mode these are C' itself: p = C'[.][g], q = s_g C'[.][g ^ 12].
+                    k3[j][h] = ts[ws_index<16>(row, g)];
+                    k2[j][h] = flip_sign(ts[ws_index<16>(row, g ^ 12)], VJP ? sg_neg : (sg_neg ^ NEG));
+                    k1[j][h] = 0.0;
+                }
+#pragma unroll
+                for (int kk = 0; kk < 2 && !VJP; ++kk) {
+                    const int m = t4 + 4 * kk;
+                    bu[j][kk] = xs[ws_index<16>(n0 + g, m)];
+                    bv[j][kk] = flip_sign(xs[ws_index<16>(n0 + g, m ^ 12)], kk ? NEG : 0u);
                 }
             }
+            if (k > 0) gemm2();
+            // GEMM 1 transposed of tile k: K[m' = g][row n0 + 2 t4 + h].
+#pragma unroll
+            for (int j = 0; j < GP && !VJP; ++j)
+#pragma unroll
+                for (int kk = 0; kk < 2; ++kk) {
+                    mma_8x8x4(k1[j], wk1[kk], bu[j][kk] - bv[j][kk]);
+                    mma_8x8x4(k2[j], wk2[kk], bu[j][kk]);
+                    mma_8x8x4(k3[j], wk3[kk], bv[j][kk]);
+                }
+#pragma unroll
+            for (int j = 0; j < GP; ++j)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const double r0 = VJP ? k3[j][h] : k1[j][h] + k3[j][h];
+                    const double r1 = VJP ? k2[j][h] : -(k1[j][h] + k2[j][h]);
+                    sq = fma(r0, r0, sq);
+                    sq = fma(r1, r1, sq);
+                    worst_exp = max(worst_exp, max(exponent_bits(r0), exponent_bits(r1)));
+                    pp[j][h] = r0;
+                    pq[j][h] = r1;
+                    pu[j][h] = cu[j][h];
+                    pv[j][h] = cv[j][h];
+                }
+            // Every value read from the stage has been used: release it.
             if (k + kWsStages < K) named_arrive(kBarEmpty + st, kWsThreads);
         }
+        if (K > 0) gemm2();
     } else {
         // ------------------------------------------------------------ consumers
         const int cw = warp - kWsProducers / 32;
@@ -896,21 +933,7 @@ rep_ws_kernel(const RepDevice rep, const double *__restrict__ X, const double *_
         // The complex-linear part of G' in the original columns: entry (m, m')
         // carries P / 2, (m, m' ^ 12) -s_m' Q / 2, (m ^ 12, m') s_m Q / 2 and
         // (m ^ 12, m' ^ 12) s_m s_m' P / 2 (halving is exact).
-        const int cw = warp - kWsProducers / 32;
-        const int g = lane >> 2, t4 = lane & 3;
-        double *gw = Gs + cw * D * D;
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int m = g, mp = 2 * t4 + i;
-            const double m1 = c3[0][0][i] + c3[0][1][i], m2 = c3[1][0][i] + c3[1][1][i];
-            const double m3 = c3[2][0][i] + c3[2][1][i];
-            const double P = 0.5 * (m1 - m3), Q = 0.5 * (m1 - m2);
-            const unsigned sm = (m & 4) ? 0x80000000u : 0u, sp = (mp & 4) ? 0x80000000u : 0u;
-            gw[m * D + mp] = P;
-            gw[m * D + (mp ^ 12)] = flip_sign(Q, sp ^ 0x80000000u);
-            gw[(m ^ 12) * D + mp] = flip_sign(Q, sm);
-            gw[(m ^ 12) * D + (mp ^ 12)] = flip_sign(P, sm ^ sp);
-        }
+        ws_store_complex_partials(c3, Gs + (warp - kWsProducers / 32) * D * D);
     } else if (warp >= kWsProducers / 32) {
         const int cw = warp - kWsProducers / 32;
         const int g = lane >> 2, t4 = lane & 3;
@@ -1281,7 +1304,8 @@ cudaError_t launch_rep_forward_impl(const RepDevice &rep, const double *X, const
 // producer thread 0 waits on it before reloading the stage, together with
 // bulk wait_group.read for the residual store). Every wait is bounded; a wait
 // that gives up poisons the CTA's remaining residuals and its record.
-template <int D, int S>
+// CPLX: GEMM 2 in the complex (3M) form, in the order of rep_ws_kernel<VJP, CPLX>.
+template <int D, int S, bool CPLX = false>
 __global__ void __launch_bounds__(kWsThreads, SgdPipe::CTAS_PER_SM)
 rep_sgd_kernel(const RepDevice rep, const double *__restrict__ X, const double *__restrict__ T,
                const double *__restrict__ W, size_t batch, double *R, double *__restrict__ records) {
@@ -1328,6 +1352,11 @@ rep_sgd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
         for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int i = 0; i < (D == 16 ? 4 : 2); ++i) gacc[p][h][i] = 0.0;
+    double c3[3][2][2];  // CPLX: M1, M2, M3 per k slice parity h
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) c3[a][h][0] = c3[a][h][1] = 0.0;
     double sq = 0.0;
     unsigned worst_exp = 0u;
 
@@ -1494,8 +1523,29 @@ rep_sgd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
                 if (!mbar_wait(&resid[st], (unsigned)((j / NST) & 1))) atomicOr(&s_gave_up, 1u);
                 const double *xs = stages + st * STAGE;
                 const double *rs = xs + 2 * TILE;
+                if constexpr (CPLX) {
+                    const unsigned sg_neg = (g & 4) ? 0x80000000u : 0u;
 #pragma unroll
-                for (int jj = 0; jj < G::GPW; jj += 2) {
+                    for (int jj = 0; jj < G::GPW; ++jj) {
+                        const int n0 = (cw * G::GPW + jj) * 8;
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int row = n0 + 2 * t4 + h;
+                            const double p = rs[ws_index<16>(row, g)];
+                            const double q = flip_sign(rs[ws_index<16>(row, g ^ 12)], sg_neg);
+                            const double u = xs[ws_index<16>(row, g)];
+                            const double v = flip_sign(xs[ws_index<16>(row, g ^ 12)], sg_neg);
+                            sq = fma(p, p, sq);
+                            sq = fma(q, q, sq);
+                            worst_exp = max(worst_exp, max(exponent_bits(p), exponent_bits(q)));
+                            mma_8x8x4(c3[0][h], u + v, p);
+                            mma_8x8x4(c3[1][h], u, p + q);
+                            mma_8x8x4(c3[2][h], v, p - q);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int jj = 0; jj < G::GPW && !CPLX; jj += 2) {
                     int n0[2];
                     n0[0] = (cw * G::GPW + jj) * 8;
                     n0[1] = n0[0] + 8;
@@ -1533,7 +1583,7 @@ rep_sgd_kernel(const RepDevice rep, const double *__restrict__ X, const double *
         }
     }
     __syncthreads();
-    ws_write_record<D, S>(rep, gacc, sq, worst_exp, &s_gave_up, stages, records);
+    ws_write_record<D, S, CPLX>(rep, gacc, c3, sq, worst_exp, &s_gave_up, stages, records);
 }
 
 template <int D, int S>
@@ -1543,6 +1593,8 @@ cudaError_t launch_rep_sgd(const RepDevice &rep, const double *X, const double *
     using P = SgdPipe;
     if (rep.raw_stride != G::N || rep.D != D || rep.S != S) return cudaErrorInvalidValue;
     auto kernel = rep_sgd_kernel<D, S>;
+    if constexpr (D == 16 && S == 4)
+        if (rep.cplx) kernel = rep_sgd_kernel<16, 4, true>;
     const size_t smem = (size_t)(D * D + P::STAGES * P::ARRAYS * G::TILE) * sizeof(double) +
                         5 * P::STAGES * sizeof(uint64_t);
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
