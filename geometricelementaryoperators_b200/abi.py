@@ -164,6 +164,7 @@ SIGNATURES: dict[str, tuple] = {
     "geo_b200_trainer_attach_comm": (_I, [_P, _P]),
     "geo_b200_v8_batch_train_step": (_I, [_P, ctypes.c_uint32, ctypes.c_uint32, _P, _P, _SZ, _I, _D, _D, _D, _D, _D, _P]),
     "geo_b200_v8_batch_forward": (_I, [_P, ctypes.c_uint32, _P, _SZ, ctypes.c_uint32, _P]),
+    "geo_b200_cr_math_f64": (_I, [_I, _P, _P, _SZ, _P]),
     "geo_b200_parameter_vjp_noalloc_f64": (_I, [_U8, _I8P, _I, _P, _P, _SZ, _P, _P]),
     "geo_b200_pairwise_gp_f64": (_I, [_U8, _I8P, _P, _P, _P, _SZ, _P]),
     "geo_b200_pairwise_gp_vjp_f64": (_I, [_U8, _I8P, _P, _P, _P, _P, _P, _SZ, _P]),

@@ -19,6 +19,7 @@
 #include <mutex>
 #include <vector>
 
+#include "crmath.h"
 #include "geo_internal.h"
 #include "v8_internal.h"
 
@@ -212,14 +213,14 @@ __global__ void __launch_bounds__(kBatchThreads, kBatchCtasPerSm) batch_kernel(c
                     o1 = __popc(b1) == nd.grade ? L[b1] : 0.0;
                     break;
                 case GEO_V8_NODE_HADAMARD: o0 = mul(L[b0], R[b0]); o1 = mul(L[b1], R[b1]); break;
-                case GEO_V8_NODE_TANH: o0 = tanh(L[b0]); o1 = tanh(L[b1]); break;
+                case GEO_V8_NODE_TANH: o0 = geo::cr::tanh(L[b0]); o1 = geo::cr::tanh(L[b1]); break;
                 case GEO_V8_NODE_SIGMOID: {
                     // reference src/full_cycle_v8.c:181-190
                     const double x[2] = {L[b0], L[b1]};
                     double y[2];
                     for (int h = 0; h < 2; ++h) {
-                        if (x[h] >= 0.0) y[h] = __ddiv_rn(1.0, add(1.0, exp(-x[h])));
-                        else { const double z = exp(x[h]); y[h] = __ddiv_rn(z, add(1.0, z)); }
+                        if (x[h] >= 0.0) y[h] = __ddiv_rn(1.0, add(1.0, geo::cr::exp(-x[h])));
+                        else { const double z = geo::cr::exp(x[h]); y[h] = __ddiv_rn(z, add(1.0, z)); }
                     }
                     o0 = y[0];
                     o1 = y[1];

@@ -14,6 +14,7 @@
 
 #include <mutex>
 
+#include "crmath.h"
 #include "geo_internal.h"
 #include "v8_internal.h"
 
@@ -115,13 +116,13 @@ __global__ void __launch_bounds__(kThreads) forward_kernel(const Ctx c) {
             case GEO_V8_NODE_CLIFFORD_CONJUGATE: if (lane) out = mul(L[b], (double)map_sign(2, b)); break;
             case GEO_V8_NODE_GRADE_PROJECT: if (lane) out = (__popc(b) == (int)node->grade) ? L[b] : 0.0; break;
             case GEO_V8_NODE_HADAMARD: if (lane) out = mul(L[b], R[b]); break;
-            case GEO_V8_NODE_TANH: if (lane) out = tanh(L[b]); break;
+            case GEO_V8_NODE_TANH: if (lane) out = geo::cr::tanh(L[b]); break;
             case GEO_V8_NODE_SIGMOID:
                 if (lane) {
                     // reference src/full_cycle_v8.c:181-190
                     const double v = L[b];
-                    if (v >= 0.0) out = __ddiv_rn(1.0, add(1.0, exp(-v)));
-                    else { const double z = exp(v); out = __ddiv_rn(z, add(1.0, z)); }
+                    if (v >= 0.0) out = __ddiv_rn(1.0, add(1.0, geo::cr::exp(-v)));
+                    else { const double z = geo::cr::exp(v); out = __ddiv_rn(z, add(1.0, z)); }
                 }
                 break;
             case GEO_V8_NODE_EUCLIDEAN_NORMALIZE: {

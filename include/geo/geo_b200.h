@@ -222,6 +222,26 @@ int geo_b200_v8_batch_train_step(void *program, uint32_t input_node, uint32_t ta
 int geo_b200_v8_batch_forward(void *program, uint32_t input_node, const double *device_inputs, size_t batch,
                               uint32_t output_node, double *device_outputs);
 
+/* The graph runtime's exp and tanh (TANH nodes; SIGMOID nodes through exp,
+ * reference src/full_cycle_v8.c:181-190, 651) are correctly rounded (round to
+ * nearest, ties to even) for every binary64 argument: a table-driven
+ * double-double evaluation with Ziv's rounding test, and an exact 256-bit
+ * fixed-point evaluation when that test cannot decide. The reference calls the
+ * C library's exp and tanh; wherever those are correctly rounded the results
+ * agree bit for bit, elsewhere the value here is the closer one.
+ * geo_b200_cr_math_f64 applies one of them to `count` doubles of a device array
+ * (device_out may equal device_in), asynchronously on `stream`; the *_EXACT_PATH
+ * values run the fixed-point evaluation for every argument it covers (a check
+ * of that path). */
+typedef enum {
+    GEO_B200_CR_EXP = 0,
+    GEO_B200_CR_TANH = 1,
+    GEO_B200_CR_EXP_EXACT_PATH = 2,
+    GEO_B200_CR_TANH_EXACT_PATH = 3
+} geo_b200_cr_function_t;
+geo_b200_status_t geo_b200_cr_math_f64(int function, const double *device_in, double *device_out, size_t count,
+                                       cudaStream_t stream);
+
 /* ---- 2c. parameter VJP that allocates nothing -------------------------- */
 
 /* This entry point has no counterpart in the reference.

@@ -36,6 +36,23 @@ OUT = pathlib.Path(__file__).resolve().parent / "batch_gp_golden.npz"
 V8_CASES = [(2, 0), (3, 0), (4, 1), (5, 1), (6, 0), (6, 3)]
 
 
+def composed_batch_cases(ref, data: dict) -> None:
+    """v8cb_*: 3 SGD and 3 Adam steps of the all-node-kinds graph over 9 samples."""
+    for n, q in [(2, 0), (3, 1), (4, 0), (5, 2), (6, 0), (6, 3)]:
+        sig = canonical_signature(n, q)
+        N = 1 << n
+        values = {"input": orc.v8_mv_fill(n, 3 + n + q), "target": orc.v8_mv_fill(n, 11 + 2 * n + q),
+                  "w1": orc.v8_mv_fill(n, 19 + n + q), "w2": orc.v8_mv_fill(n, 29 + n + q)}
+        xs = splitmix_uniform(91 + n + q, (9, N))
+        ts = splitmix_uniform(92 + n + q, (9, N))
+        data[f"v8cb_n{n}q{q}_x"], data[f"v8cb_n{n}q{q}_t"] = xs, ts
+        for opt in (1, 2):
+            w1s, w2s, losses = ref.v8_composed_train(sig, values, xs, ts, opt, 1e-2, steps=3)
+            data[f"v8cb_n{n}q{q}_opt{opt}_w1"] = w1s
+            data[f"v8cb_n{n}q{q}_opt{opt}_w2"] = w2s
+            data[f"v8cb_n{n}q{q}_opt{opt}_loss"] = losses
+
+
 def main() -> None:
     if not orc.ensure_reference_built():
         raise SystemExit("the reference build (oracle/_ref) is required to make golden vectors")
@@ -96,19 +113,7 @@ def main() -> None:
             data[f"v8c_n{n}q{q}_g1"], data[f"v8c_n{n}q{q}_g2"] = g1, g2
     # Per-sample training of the all-node-kinds graph over a small batch (the
     # general path of the batched V8 step is checked against these).
-    for n, q in [(2, 0), (3, 1), (4, 0), (5, 2), (6, 0), (6, 3)]:
-        sig = canonical_signature(n, q)
-        N = 1 << n
-        values = {"input": orc.v8_mv_fill(n, 3 + n + q), "target": orc.v8_mv_fill(n, 11 + 2 * n + q),
-                  "w1": orc.v8_mv_fill(n, 19 + n + q), "w2": orc.v8_mv_fill(n, 29 + n + q)}
-        xs = splitmix_uniform(91 + n + q, (9, N))
-        ts = splitmix_uniform(92 + n + q, (9, N))
-        data[f"v8cb_n{n}q{q}_x"], data[f"v8cb_n{n}q{q}_t"] = xs, ts
-        for opt in (1, 2):
-            w1s, w2s, losses = ref.v8_composed_train(sig, values, xs, ts, opt, 1e-2, steps=3)
-            data[f"v8cb_n{n}q{q}_opt{opt}_w1"] = w1s
-            data[f"v8cb_n{n}q{q}_opt{opt}_w2"] = w2s
-            data[f"v8cb_n{n}q{q}_opt{opt}_loss"] = losses
+    composed_batch_cases(ref, data)
     np.savez_compressed(OUT, **data)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes, {len(data)} arrays)")
 

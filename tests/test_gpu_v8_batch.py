@@ -22,6 +22,7 @@ from tests.test_gpu_v8 import V8Program, _lib, mv, value
 
 pytestmark = pytest.mark.gpu
 GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "batch_gp_golden.npz"
+CRMATH_GOLDEN = pathlib.Path(__file__).resolve().parent / "golden" / "v8_crmath_golden.npz"
 CASES = [(2, 0), (3, 1), (4, 0), (5, 2), (6, 0), (6, 3)]
 
 
@@ -59,12 +60,17 @@ def _loop_step(L, prog, x_id, t_id, xs, ts, sig, n, loss_id, opt, lr=1e-2):
     return total
 
 
-# The graph's tanh and sigmoid use the device libm, which differs from glibc by
-# an ulp or two; SGD steps keep those differences at the ulp level (checked at
-# 1e-12), but Adam divides each update by the root of its second moment, which
-# amplifies them on gradient components that nearly cancel over the batch: after
-# three Adam steps the reference and the per-sample GPU runtime (geo_v8_*) agree
-# to 2e-11. The batched path itself is bit-identical to that runtime
+# The graph's tanh and sigmoid are correctly rounded here (csrc/crmath.h); the
+# reference calls the C library's, whose tanh misses the correctly rounded value
+# on about one argument in eight (exp on a few in ten thousand). SGD steps keep
+# those differences at the ulp level (checked at 1e-12), but Adam divides each
+# update by the root of its second moment, which amplifies them on gradient
+# components that nearly cancel over the batch: after three Adam steps the
+# reference and this runtime agree to ~1.3e-11, exactly the distance between the
+# reference built against the C library and the reference built against the
+# correctly rounded functions (make_v8_crmath_golden.py), which this runtime
+# meets at 1e-12 (test_general_batch_step_golden_crmath). The batched path
+# itself is bit-identical to the per-sample runtime
 # (test_general_batch_step_matches_loop_exact).
 ADAM_TOL = 1e-10
 
@@ -90,6 +96,30 @@ def test_general_batch_step_golden(n, q):
             assert tol_close(w2, g2, tol), (opt, k, max_violation(w2, g2, tol))
             assert tol_close(loss, golden[f"v8cb_n{n}q{q}_opt{opt}_loss"][k], TOL)
             assert prog.optimizer_step == k + 1
+        L.geo_v8_program_free(ctypes.byref(prog))
+
+
+@pytest.mark.parametrize("n,q", CASES)
+def test_general_batch_step_golden_crmath(n, q):
+    """The same graph and steps against the reference built with exp and tanh bound
+    to the runtime's correctly rounded functions (tests/golden/make_v8_crmath_golden.py):
+    with the nonlinearities rounded alike, SGD and Adam both meet the float64 bar."""
+    L = _lib()
+    golden = np.load(CRMATH_GOLDEN)
+    sig = canonical_signature(n, q)
+    xs, ts = golden[f"v8cb_n{n}q{q}_x"], golden[f"v8cb_n{n}q{q}_t"]
+    dx, dt = dev(xs), dev(ts)
+    for opt in (1, 2):
+        prog, ids = _composed(L, sig, _values(n, q))
+        for k in range(3):
+            st, loss = _batch_step(L, prog, ids["x"], ids["y"], dx, dt, xs.shape[0], opt)
+            assert st == 0, st
+            w1, w2 = value(L, prog, ids["p1"], n), value(L, prog, ids["p2"], n)
+            g1 = golden[f"v8cb_n{n}q{q}_opt{opt}_w1"][k]
+            g2 = golden[f"v8cb_n{n}q{q}_opt{opt}_w2"][k]
+            assert tol_close(w1, g1, TOL), (opt, k, max_violation(w1, g1, TOL))
+            assert tol_close(w2, g2, TOL), (opt, k, max_violation(w2, g2, TOL))
+            assert tol_close(loss, golden[f"v8cb_n{n}q{q}_opt{opt}_loss"][k], TOL)
         L.geo_v8_program_free(ctypes.byref(prog))
 
 
