@@ -898,6 +898,10 @@ def run_b200(args, world, rank, local):
         extras["e2e"] = {"value": batch * world / e2e_s, "unit": UNIT,
                          "h2d_bytes_per_step": 2 * batch * 64 * 8 * world, "d2h_bytes_per_step": 8 * world,
                          "timing": "host wall clock around the synchronous host-buffer call, max over ranks",
+                         # the reference CUDA harness's classes (benchmarks/bench_v8_cuda.cu:124-135):
+                         # `value` is its "resident" class, this one its "transfer_compute" (inputs
+                         # uploaded every step; here the loss is also read back)
+                         "timing_class": "transfer_compute",
                          "steps": e2e_steps}
         del hx, ht
 
