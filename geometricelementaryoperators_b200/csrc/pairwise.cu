@@ -21,6 +21,7 @@
 
 #include "geo/geo_b200.h"
 #include "geo_runtime.h"
+#include "pair_tables_gen.h"
 
 namespace {
 
@@ -795,6 +796,309 @@ cudaError_t launch_f64_tma_dispatch(int neg, const CUtensorMap &ma, const CUtens
     return e;
 }
 
+
+// ---- float64 n = 6 through the matrix representation (canonical D = 16 algebras)
+// y = a b as Y' = A' rho(b) (geo::make_pair_tables: 1024 multiply-adds per
+// product instead of 4096) for Cl(6,0), Cl(5,1), Cl(2,4) and Cl(1,5), whose
+// tables are compile-time data (pair_tables_gen.h, written by
+// gen_pair_tables.cpp from the same host code): blade offsets are immediates
+// and signs are negations inside the multiply-adds. A product is handled by four
+// lanes of a warp, lane l one kept row: it forms its 16 coefficients Ah[m] of a
+// from broadcast reads of the raw row (the four lanes read the same words; the
+// lane enters only through the signs (-1)^{popc(c & l)}, applied as exact +-1
+// multiply-adds), then for every group g of b a Walsh transform of the
+// lane-signed members and 16 multiply-adds into Yh[u]; a Walsh transform of
+// Yh[g] across the four lanes (shfl.xor) leaves output blade[g][c] in lane c.
+// Operand rows arrive by 512-byte bulk copies into rows of 66 doubles (528 B):
+// the eight rows a warp reads at once fall in eight distinct bank pairs, so
+// every broadcast read is one wavefront. The ring (2 stages, producer warp,
+// full / empty mbarriers, bounded waits, abort protocol) is the one of
+// pairwise_f64_n6_tma_kernel; outputs are written over the product's a row of
+// the (last) stage and leave by one 512-byte bulk store per row.
+struct PairTablesC {
+    unsigned char blade[16][4], xa[16][4], xb[16][4], post[16][4], chi[16][2];
+};
+constexpr PairTablesC kPairTables[4][4] = GEO_PAIR_TABLES_INIT;
+
+constexpr int kPrRows = 32;                  // products per tile
+constexpr int kPrPitch = 66;                 // doubles per staged row
+constexpr int kPrCompute = 4;                // compute warps, 8 products each
+constexpr int kPrThreads = 32 * (kPrCompute + 1);
+constexpr int kPrStages = 2;
+constexpr int kPrStage = 2 * kPrRows * kPrPitch;   // doubles per stage (a rows, b rows)
+constexpr size_t kPrSmem = (size_t)kPrStages * kPrStage * sizeof(double) + 16;
+
+template <int... I, typename F>
+__device__ __forceinline__ void static_for_seq(std::integer_sequence<int, I...>, F &&f) {
+    (f(std::integral_constant<int, I>{}), ...);
+}
+template <int N, typename F>
+__device__ __forceinline__ void static_for(F &&f) {
+    static_for_seq(std::make_integer_sequence<int, N>{}, f);
+}
+
+__device__ __forceinline__ void bulk_load_1d(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_store_1d(void *dst, const void *src, unsigned bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(dst), "r"(smem_u32(src)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+template <int SI, int REV, int PRODUCTS, bool STARVE = false>
+__global__ void __launch_bounds__(kPrThreads, 3)
+pairwise_rep_kernel(const double *__restrict__ a1, const double *__restrict__ b1, const double *__restrict__ a2,
+                    const double *__restrict__ b2, double *__restrict__ out, size_t batch, uint32_t wait_limit,
+                    uint32_t opaque_zero) {
+    extern __shared__ unsigned char pr_raw[];
+    __shared__ __align__(8) uint64_t full[kPrStages], empty[kPrStages];
+    __shared__ volatile int s_abort;
+    double *base = reinterpret_cast<double *>(((uintptr_t)pr_raw + 15) & ~(uintptr_t)15);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t tiles = (batch + kPrRows - 1) / kPrRows;
+    const int K = (size_t)blockIdx.x < tiles ? (int)((tiles - 1 - blockIdx.x) / gridDim.x + 1) : 0;
+    if (tid == 0) {
+        for (int st = 0; st < kPrStages; ++st) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_u32(&full[st])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(&empty[st])), "r"(kPrCompute)
+                         : "memory");
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        s_abort = 0;
+    }
+    __syncthreads();
+    if (warp == kPrCompute) {
+        // ---- producer: one thread keeps the ring full (row copies of a and b)
+        if (lane == 0 && !STARVE) {
+            int issued = 0;
+            for (int v = 0; v < K * PRODUCTS; ++v) {
+                const int st = v % kPrStages;
+                if (v >= kPrStages &&
+                    !tma_bounded_wait(&empty[st], (unsigned)((v / kPrStages - 1) & 1), wait_limit)) {
+                    s_abort = 1;
+                    atomicAdd(&g_pairwise_tma_wait_failures, 1u);
+                }
+                if (s_abort) break;
+                double *sa = base + st * kPrStage;
+                const size_t row0 = (blockIdx.x + (size_t)(v / PRODUCTS) * gridDim.x) * kPrRows;
+                const int rows = batch - row0 < (size_t)kPrRows ? (int)(batch - row0) : kPrRows;
+                const bool second = v % PRODUCTS != 0;
+                const double *ga = (second ? a2 : a1) + row0 * 64;
+                const double *gb = (second ? b2 : b1) + row0 * 64;
+                // (also orders the compute warps' writes of the stage before the reload)
+                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(&full[st])),
+                             "r"((unsigned)(2 * rows * 512))
+                             : "memory");
+                for (int r = 0; r < rows; ++r) {
+                    bulk_load_1d(sa + r * kPrPitch, ga + r * 64, 512u, &full[st]);
+                    bulk_load_1d(sa + (kPrRows + r) * kPrPitch, gb + r * 64, 512u, &full[st]);
+                }
+                issued = v + 1;
+            }
+            for (int v = issued > kPrStages ? issued - kPrStages : 0; v < issued; ++v)
+                (void)tma_bounded_wait(&full[v % kPrStages], (unsigned)((v / kPrStages) & 1), wait_limit);
+        }
+        return;
+    }
+    // ---- compute warps
+    const int ps = lane >> 2, l = lane & 3;
+    const int prow = warp * 8 + ps;  // product row within the tile
+    // The lane's signs (-1)^{popc(c & l)}: member 1 by s1, member 2 by s2, member 3
+    // by s1 s2, as multiplies by +-1 inside fused multiply-adds (exact: each sum
+    // rounds as a plain add).
+    const double s1 = (l & 1) ? -1.0 : 1.0, s2 = (l & 2) ? -1.0 : 1.0;
+    for (int k = 0; k < K; ++k) {
+        double yh[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) yh[u] = 0.0;
+        bool failed = false;
+        int last_st = 0;
+#pragma unroll 1
+        for (int pp = 0; pp < PRODUCTS; ++pp) {
+            const int v = k * PRODUCTS + pp;
+            const int st = v % kPrStages;
+            const bool ok = tma_bounded_wait(&full[st], (unsigned)((v / kPrStages) & 1), wait_limit);
+            if (__any_sync(0xffffffffu, !ok) || s_abort) {
+                failed = true;
+                break;
+            }
+            const double *ra = base + st * kPrStage + prow * kPrPitch;
+            const double *rb = ra + kPrRows * kPrPitch;
+            // Reads of a group's members depend (through opaque_zero, so by a zero) on a
+            // word of the previous group: the loads run about one group ahead instead of
+            // all 64 of a phase being issued at once into registers.
+            unsigned dep = 0u;
+            double ah[16];
+            static_for<16>([&](auto mI) {
+                constexpr int m = decltype(mI)::value;
+                const double *pa = ra + dep;
+                double w[4];
+                static_for<4>([&](auto cI) {
+                    constexpr int c = decltype(cI)::value;
+                    constexpr int blade = kPairTables[SI][REV].blade[m][c];
+                    constexpr bool neg = kPairTables[SI][REV].xa[m][c] != 0;
+                    const double x = pa[blade];
+                    w[c] = neg ? -x : x;
+                });
+                dep = opaque_zero & (unsigned)__double2loint(w[0]);
+                // (w0 + s1 w1) + (s2 w2 + s1 s2 w3)
+                ah[m] = fma(s2, fma(s1, w[3], w[2]), fma(s1, w[1], w[0]));
+            });
+            static_for<16>([&](auto gI) {
+                constexpr int g = decltype(gI)::value;
+                const double *pb = rb + dep;
+                double w[4];
+                static_for<4>([&](auto cI) {
+                    constexpr int c = decltype(cI)::value;
+                    constexpr int blade = kPairTables[SI][REV].blade[g][c];
+                    constexpr bool neg = kPairTables[SI][REV].xb[g][c] != 0;
+                    const double x = pb[blade];
+                    w[c] = neg ? -x : x;
+                });
+                dep = opaque_zero & (unsigned)__double2loint(w[0]);
+                // Walsh transform of (w0, s1 w1, s2 w2, s1 s2 w3)
+                const double e0 = fma(s1, w[1], w[0]), f0 = fma(-s1, w[1], w[0]);
+                const double e1 = fma(s1, w[3], w[2]), f1 = fma(-s1, w[3], w[2]);
+                const double bt[4] = {fma(s2, e1, e0), fma(s2, f1, f0), fma(-s2, e1, e0), fma(-s2, f1, f0)};
+                static_for<16>([&](auto uI) {
+                    constexpr int u = decltype(uI)::value;
+                    constexpr int uh = u >> 2;
+                    constexpr bool h1 = kPairTables[SI][REV].chi[g][0] != 0;
+                    constexpr bool h2 = kPairTables[SI][REV].chi[g][1] != 0;
+                    constexpr bool neg = uh == 0 ? false : uh == 1 ? h1 : uh == 2 ? h2 : h1 != h2;
+                    yh[u] = fma(ah[g ^ u], neg ? -bt[u & 3] : bt[u & 3], yh[u]);
+                });
+            });
+            __syncwarp();
+            last_st = st;
+            if (pp + 1 < PRODUCTS && lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(&empty[st])) : "memory");
+        }
+        const size_t row0 = (blockIdx.x + (size_t)k * gridDim.x) * kPrRows;
+        if (failed) {
+            // Abort: NaN into this warp's product rows of tiles k..K-1 (plain stores).
+            if (lane == 0) {
+                s_abort = 1;
+                atomicAdd(&g_pairwise_tma_wait_failures, 1u);
+            }
+            for (int j = k; j < K; ++j) {
+                const size_t row = (blockIdx.x + (size_t)j * gridDim.x) * kPrRows + (size_t)prow;
+                if (row < batch)
+                    for (int c = 0; c < 16; ++c) out[row * 64 + 16 * l + c] = __longlong_as_double(0x7ff8000000000000ll);
+            }
+            break;
+        }
+        // Walsh transform of Yh[g] across the four lanes of the product.
+#pragma unroll
+        for (int h = 1; h < 4; h <<= 1) {
+            const double sg = (l & h) ? -1.0 : 1.0;
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const double o = __shfl_xor_sync(0xffffffffu, yh[u], h);
+                yh[u] = fma(sg, yh[u], o);
+            }
+        }
+        // Outputs over this product's a row of the last stage (no lane reads it any
+        // more): lane l holds blade[g][l] of every group g.
+        double *ro = base + last_st * kPrStage + prow * kPrPitch;
+        static_for<16>([&](auto gI) {
+            constexpr int g = decltype(gI)::value;
+            constexpr int B0 = kPairTables[SI][REV].blade[g][0], B1 = kPairTables[SI][REV].blade[g][1];
+            constexpr int B2 = kPairTables[SI][REV].blade[g][2], B3 = kPairTables[SI][REV].blade[g][3];
+            constexpr bool P0 = kPairTables[SI][REV].post[g][0] != 0, P1 = kPairTables[SI][REV].post[g][1] != 0;
+            constexpr bool P2 = kPairTables[SI][REV].post[g][2] != 0, P3 = kPairTables[SI][REV].post[g][3] != 0;
+            const int bl = l == 0 ? B0 : l == 1 ? B1 : l == 2 ? B2 : B3;
+            const bool pn = l == 0 ? P0 : l == 1 ? P1 : l == 2 ? P2 : P3;
+            ro[bl] = (pn ? -yh[g] : yh[g]) * 0.25;  // exact
+        });
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+            for (int q = 0; q < 8; ++q) {
+                const size_t row = row0 + (size_t)(warp * 8 + q);
+                if (row < batch)
+                    bulk_store_1d(out + row * 64, base + last_st * kPrStage + (warp * 8 + q) * kPrPitch, 512u);
+            }
+            asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+            // The stage is reloaded only after the stores have read it.
+            asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(&empty[last_st])) : "memory");
+        }
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+}
+
+// Index of a canonical D = 16 signature in the generated tables, or -1.
+int pair_table_index(const int8_t *signature) {
+    unsigned mask = 0;
+    for (unsigned a = 0; a < 6; ++a)
+        if (signature[a] < 0) mask |= 1u << a;
+    switch (mask) {
+        case 0x00u: return 0;  // Cl(6,0)
+        case 0x20u: return 1;  // Cl(5,1)
+        case 0x3Cu: return 2;  // Cl(2,4)
+        case 0x3Eu: return 3;  // Cl(1,5)
+        default: return -1;
+    }
+}
+
+template <int SI, int REV, int PRODUCTS, bool STARVE = false>
+cudaError_t launch_pair_rep_t(const double *a1, const double *b1, const double *a2, const double *b2, double *out,
+                              size_t batch, cudaStream_t stream, uint32_t wait_limit) {
+    auto kernel = pairwise_rep_kernel<SI, REV, PRODUCTS, STARVE>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrSmem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kPrThreads, kPrSmem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) per_sm = 1;
+    const size_t tiles = (batch + kPrRows - 1) / kPrRows;
+    size_t grid = (size_t)geo::device_sm_count() * (size_t)per_sm;
+    if (grid > tiles) grid = tiles;
+    kernel<<<(unsigned)grid, kPrThreads, kPrSmem, stream>>>(a1, b1, a2, b2, out, batch, wait_limit, 0u);
+    return cudaGetLastError();
+}
+
+template <int SI>
+cudaError_t launch_pair_rep_si(int rev, int products, const double *a1, const double *b1, const double *a2,
+                               const double *b2, double *out, size_t batch, cudaStream_t stream) {
+    if (products == 2) return launch_pair_rep_t<SI, 0, 2>(a1, b1, a2, b2, out, batch, stream, kTmaWaitLimit);
+    switch (rev) {
+        case 1: return launch_pair_rep_t<SI, 1, 1>(a1, b1, a2, b2, out, batch, stream, kTmaWaitLimit);
+        case 2: return launch_pair_rep_t<SI, 2, 1>(a1, b1, a2, b2, out, batch, stream, kTmaWaitLimit);
+        default: return launch_pair_rep_t<SI, 0, 1>(a1, b1, a2, b2, out, batch, stream, kTmaWaitLimit);
+    }
+}
+
+// out = left right (or + left2 right2, the JVP) through the representation;
+// false when it does not apply (a canonical D = 16 signature, 16-byte aligned
+// operands; the JVP without operand reversal).
+bool launch_pairwise_rep(const int8_t *signature, const double *left, const double *right, double *out, size_t batch,
+                         cudaStream_t stream, cudaError_t *err, bool rev_left, bool rev_right, const double *left2,
+                         const double *right2) {
+    const bool two = left2 != nullptr && right2 != nullptr;
+    if (((uintptr_t)left | (uintptr_t)right | (uintptr_t)out) & 15u) return false;
+    if (two && (((uintptr_t)left2 | (uintptr_t)right2) & 15u || rev_left || rev_right)) return false;
+    if (rev_left && rev_right) return false;
+    const int si = pair_table_index(signature);
+    if (si < 0) return false;
+    const int rev = (rev_left ? 1 : 0) | (rev_right ? 2 : 0);
+    const double *a2 = two ? left2 : left, *b2 = two ? right2 : right;
+    const int products = two ? 2 : 1;
+    switch (si) {
+        case 0: *err = launch_pair_rep_si<0>(rev, products, left, right, a2, b2, out, batch, stream); break;
+        case 1: *err = launch_pair_rep_si<1>(rev, products, left, right, a2, b2, out, batch, stream); break;
+        case 2: *err = launch_pair_rep_si<2>(rev, products, left, right, a2, b2, out, batch, stream); break;
+        default: *err = launch_pair_rep_si<3>(rev, products, left, right, a2, b2, out, batch, stream); break;
+    }
+    return true;
+}
+
 // float64 n = 6 forward on the TMA kernel, out = left right, or with left2 and
 // right2 given out = left right + left2 right2 in one pass (the JVP); false when
 // it does not apply (unaligned operands, no tensor-map encoder, sign table that
@@ -803,6 +1107,9 @@ bool launch_pairwise_f64_fast(const geo::SignPlan &plan, const int8_t *signature
                               const double *right, double *out, size_t batch, cudaStream_t stream, cudaError_t *err,
                               bool rev_left = false, bool rev_right = false, const double *left2 = nullptr,
                               const double *right2 = nullptr) {
+    if (plan.blades == 64 && launch_pairwise_rep(signature, left, right, out, batch, stream, err, rev_left, rev_right,
+                                                 left2, right2))
+        return true;
     const bool two = left2 != nullptr && right2 != nullptr;
     if (plan.blades != 64 || ((uintptr_t)left | (uintptr_t)right | (uintptr_t)out) & 15u) return false;
     if (two && ((uintptr_t)left2 | (uintptr_t)right2) & 15u) return false;
@@ -953,6 +1260,13 @@ extern "C" geo_b200_status_t geo_b200_pairwise_wait_selftest(int precision, void
     cudaError_t e = cudaSuccess;
     if (precision == 64) {
         double *out = static_cast<double *>(device_out);
+        // The representation kernel first (Cl(6,0) tables), then the direct one.
+        e = launch_pair_rep_t<0, 0, 1, true>(out, out, out, out, out, batch, stream, wait_limit);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return from_cuda(e);
+        unsigned first = 0;
+        st = geo_b200_pairwise_wait_failures(&first, 1);
+        if (st != GEO_B200_TIMEOUT) return st == GEO_B200_OK ? GEO_B200_RUNTIME_FAILURE : st;
         CUtensorMap m;
         if (!encode_rows_f64(&m, out, batch)) return GEO_B200_INVALID_ARGUMENT;
         F64BlockSigns signs;

@@ -426,3 +426,129 @@ const RepDevice *cached_rep_device(uint8_t dimension, const int8_t *signature, b
 }
 
 }  // namespace geo
+
+namespace geo {
+
+bool make_pair_tables(const RepPlan &p, const int8_t *signature, bool rev_a, bool rev_b, PairTables *out) {
+    std::memset(out, 0, sizeof(*out));
+    if (!p.valid || p.dimension != 6 || p.D != 16 || p.S != 4 || p.side != 0) return false;
+    int kern[4], nk = 0;  // the blades with x-mask 0
+    for (int A = 0; A < 64; ++A)
+        if (p.xm[A] == 0) {
+            if (nk == 4) return false;
+            kern[nk++] = A;
+        }
+    if (nk != 4 || kern[0] != 0) return false;
+    const int k1 = kern[1];
+    int k2 = -1;
+    for (int i = 2; i < 4; ++i)
+        if (p.zm[kern[i]] != p.zm[k1]) {
+            k2 = kern[i];
+            break;
+        }
+    if (k2 < 0) return false;
+    unsigned z[4] = {p.zm[k1], p.zm[k2], 0, 0};
+    if (z[0] == 0 || z[1] == 0 || z[0] == z[1]) return false;
+    auto spans = [&](unsigned v, int n) {
+        for (unsigned c = 0; c < (1u << n); ++c) {
+            unsigned acc = 0;
+            for (int i = 0; i < n; ++i)
+                if ((c >> i) & 1u) acc ^= z[i];
+            if (acc == v) return true;
+        }
+        return false;
+    };
+    int nz = 2;  // extend {z1, z2} to a basis with unit vectors
+    for (unsigned e = 1; e < 16 && nz < 4; e <<= 1)
+        if (!spans(e, nz)) z[nz++] = e;
+    if (nz != 4) return false;
+    int coord[16];  // z -> its coordinates in the basis z[0..3]
+    for (int v = 0; v < 16; ++v) coord[v] = -1;
+    for (unsigned c = 0; c < 16; ++c) {
+        unsigned acc = 0;
+        for (int i = 0; i < 4; ++i)
+            if ((c >> i) & 1u) acc ^= z[i];
+        coord[acc] = (int)c;
+    }
+    for (int v = 0; v < 16; ++v)
+        if (coord[v] < 0) return false;
+    auto T = [&](unsigned x) {
+        unsigned u = 0;
+        for (int i = 0; i < 4; ++i) u |= (unsigned)(popc(z[i] & x) & 1) << i;
+        return u;
+    };
+    auto kappa = [&](int c) { return ((c & 1) ? k1 : 0) ^ ((c & 2) ? k2 : 0); };
+    auto par = [](unsigned v) { return (popc(v) & 1) != 0; };
+    const uint32_t NEG = 0x80000000u;
+    bool seen[16] = {};
+    for (int A = 0; A < 64; ++A) {
+        const unsigned g = T(p.xm[A]);
+        if (seen[g]) continue;
+        seen[g] = true;
+        const int B0 = A ^ kappa(coord[p.zm[A]] & 3);
+        const unsigned zb = (unsigned)coord[p.zm[B0]];
+        if ((zb & 3u) != 0u || T(p.xm[B0]) != g) return false;
+        for (int c = 0; c < 4; ++c) {
+            const int B = B0 ^ kappa(c);
+            if (T(p.xm[B]) != g || (unsigned)coord[p.zm[B]] != (zb ^ (unsigned)c)) return false;
+            out->blade[g][c] = (uint8_t)B;
+            const bool sneg = p.sg[B] < 0;
+            const bool self = sign_rule((uint8_t)B, (uint8_t)B, signature, 6) < 0;
+            out->xa[g][c] = (sneg != (rev_a && self)) != (par((unsigned)c & (g & 3u)) != par(zb & g)) ? NEG : 0u;
+            out->xb[g][c] = (sneg != (rev_b && self)) ? NEG : 0u;
+            out->post[g][c] = (sneg != par(zb & g)) != par((unsigned)c & (g & 3u)) ? NEG : 0u;
+        }
+        const uint32_t h1 = (zb & 4u) ? NEG : 0u, h2 = (zb & 8u) ? NEG : 0u;
+        out->chi[g][0] = h1;
+        out->chi[g][1] = h2;
+        out->chi[g][2] = h1 ^ h2;
+    }
+    for (int g = 0; g < 16; ++g)
+        if (!seen[g]) return false;
+    return true;
+}
+
+void pair_product_host(const PairTables &t, const double *a, const double *b, double *y) {
+    double yh[4][16];
+    auto flip = [](double v, uint32_t m) { return m ? -v : v; };
+    for (int l = 0; l < 4; ++l) {
+        uint32_t xl[4];
+        for (int c = 0; c < 4; ++c) xl[c] = (popc((unsigned)(c & l)) & 1) ? 0x80000000u : 0u;
+        double ah[16];
+        for (int m = 0; m < 16; ++m) {
+            double w[4];
+            for (int c = 0; c < 4; ++c) w[c] = flip(a[t.blade[m][c]], t.xa[m][c] ^ xl[c]);
+            ah[m] = (w[0] + w[1]) + (w[2] + w[3]);
+        }
+        for (int u = 0; u < 16; ++u) yh[l][u] = 0.0;
+        for (int g = 0; g < 16; ++g) {
+            double w[4];
+            for (int c = 0; c < 4; ++c) w[c] = flip(b[t.blade[g][c]], t.xb[g][c] ^ xl[c]);
+            for (int h = 1; h < 4; h <<= 1)
+                for (int c = 0; c < 4; ++c)
+                    if (!(c & h)) {
+                        const double u0 = w[c], v0 = w[c | h];
+                        w[c] = u0 + v0;
+                        w[c | h] = u0 - v0;
+                    }
+            for (int u = 0; u < 16; ++u) {
+                const int uh = u >> 2;
+                const double bv = uh == 0 ? w[u & 3] : flip(w[u & 3], t.chi[g][uh - 1]);
+                yh[l][u] += ah[g ^ u] * bv;
+            }
+        }
+    }
+    for (int g = 0; g < 16; ++g) {
+        double w[4] = {yh[0][g], yh[1][g], yh[2][g], yh[3][g]};
+        for (int h = 1; h < 4; h <<= 1)
+            for (int c = 0; c < 4; ++c)
+                if (!(c & h)) {
+                    const double u0 = w[c], v0 = w[c | h];
+                    w[c] = u0 + v0;
+                    w[c | h] = u0 - v0;
+                }
+        for (int c = 0; c < 4; ++c) y[t.blade[g][c]] = flip(w[c], t.post[g][c]) * 0.25;
+    }
+}
+
+}  // namespace geo

@@ -59,4 +59,30 @@ bool make_rep_plan(RepPlan *out, uint8_t dimension, const int8_t *signature, int
 // by tests): dense rho(e_A) entry, the kept-entry matrix P, and W'.
 int rep_entry(const RepPlan &p, int blade, int i, int j);
 
+// Tables of the pairwise product y = a b (both operands vary) through the
+// representation, for the n = 6 algebras with D = 16, S = 4 (right-side plan):
+// Y' = A' rho(b), A' = S kept rows of rho(a), 1024 multiply-adds instead of 4096.
+//
+// The blades with x-mask 0 form K = {0, k1, k2, k1 ^ k2}; with z1, z2 their z-masks
+// extended to a basis z1..z4 of GF(2)^4, the index space is relabelled by
+// u = T j, (T j)_i = popc(z_i & j) mod 2, so z . j = z' . u with z' the
+// coordinates of z in that basis. Then k1, k2 have z' = e0, e1, a group g (the
+// four blades of one x-mask, relabelled g = T x) is B0 ^ {0, k1, k2, k1 ^ k2} with
+// z'(B0) chosen free of the low two bits, and member c has z' = z'(B0) ^ c. The
+// kept rows are T^-1 {0, 1, 2, 3}. Lane l (kept row l) of a product forms
+//   Ah[m] = sum_c (-1)^{xa[m][c] + popc(c & l)} a[blade[m][c]]
+//   bt_g  = Walsh transform over c of (-1)^{xb[g][c] + popc(c & l)} b[blade[g][c]]
+//   Yh[u] = sum_g Ah[g ^ u] (-1)^{chi(g, u >> 2)} bt_g[u & 3]
+// and a Walsh transform of Yh[g] over the four lanes leaves in lane c
+// 4 (-1)^{post[g][c]} y[blade[g][c]] (sign words: bit 31).
+struct PairTables {
+    uint8_t blade[16][4];
+    uint32_t xa[16][4], xb[16][4], post[16][4];
+    uint32_t chi[16][3];  // sign words for u's high bits 1, 2, 3
+};
+// rev_a / rev_b multiply operand blade m by s(m, m) (the operands of the VJP products).
+bool make_pair_tables(const RepPlan &p, const int8_t *signature, bool rev_a, bool rev_b, PairTables *out);
+// The same arithmetic on the host (the check of the tables; y = a b).
+void pair_product_host(const PairTables &t, const double *a, const double *b, double *y);
+
 }  // namespace geo
