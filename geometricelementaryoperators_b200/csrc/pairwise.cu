@@ -852,8 +852,7 @@ __device__ __forceinline__ void bulk_store_1d(void *dst, const void *src, unsign
 template <int SI, int REV, int PRODUCTS, bool STARVE = false>
 __global__ void __launch_bounds__(kPrThreads, 3)
 pairwise_rep_kernel(const double *__restrict__ a1, const double *__restrict__ b1, const double *__restrict__ a2,
-                    const double *__restrict__ b2, double *__restrict__ out, size_t batch, uint32_t wait_limit,
-                    uint32_t opaque_zero) {
+                    const double *__restrict__ b2, double *__restrict__ out, size_t batch, uint32_t wait_limit) {
     extern __shared__ unsigned char pr_raw[];
     __shared__ __align__(8) uint64_t full[kPrStages], empty[kPrStages];
     __shared__ volatile int s_abort;
@@ -929,14 +928,10 @@ pairwise_rep_kernel(const double *__restrict__ a1, const double *__restrict__ b1
             }
             const double *ra = base + st * kPrStage + prow * kPrPitch;
             const double *rb = ra + kPrRows * kPrPitch;
-            // Reads of a group's members depend (through opaque_zero, so by a zero) on a
-            // word of the previous group: the loads run about one group ahead instead of
-            // all 64 of a phase being issued at once into registers.
-            unsigned dep = 0u;
             double ah[16];
             static_for<16>([&](auto mI) {
                 constexpr int m = decltype(mI)::value;
-                const double *pa = ra + dep;
+                const double *pa = ra;
                 double w[4];
                 static_for<4>([&](auto cI) {
                     constexpr int c = decltype(cI)::value;
@@ -945,13 +940,12 @@ pairwise_rep_kernel(const double *__restrict__ a1, const double *__restrict__ b1
                     const double x = pa[blade];
                     w[c] = neg ? -x : x;
                 });
-                dep = opaque_zero & (unsigned)__double2loint(w[0]);
                 // (w0 + s1 w1) + (s2 w2 + s1 s2 w3)
                 ah[m] = fma(s2, fma(s1, w[3], w[2]), fma(s1, w[1], w[0]));
             });
             static_for<16>([&](auto gI) {
                 constexpr int g = decltype(gI)::value;
-                const double *pb = rb + dep;
+                const double *pb = rb;
                 double w[4];
                 static_for<4>([&](auto cI) {
                     constexpr int c = decltype(cI)::value;
@@ -960,7 +954,6 @@ pairwise_rep_kernel(const double *__restrict__ a1, const double *__restrict__ b1
                     const double x = pb[blade];
                     w[c] = neg ? -x : x;
                 });
-                dep = opaque_zero & (unsigned)__double2loint(w[0]);
                 // Walsh transform of (w0, s1 w1, s2 w2, s1 s2 w3)
                 const double e0 = fma(s1, w[1], w[0]), f0 = fma(-s1, w[1], w[0]);
                 const double e1 = fma(s1, w[3], w[2]), f1 = fma(-s1, w[3], w[2]);
@@ -1060,7 +1053,7 @@ cudaError_t launch_pair_rep_t(const double *a1, const double *b1, const double *
     const size_t tiles = (batch + kPrRows - 1) / kPrRows;
     size_t grid = (size_t)geo::device_sm_count() * (size_t)per_sm;
     if (grid > tiles) grid = tiles;
-    kernel<<<(unsigned)grid, kPrThreads, kPrSmem, stream>>>(a1, b1, a2, b2, out, batch, wait_limit, 0u);
+    kernel<<<(unsigned)grid, kPrThreads, kPrSmem, stream>>>(a1, b1, a2, b2, out, batch, wait_limit);
     return cudaGetLastError();
 }
 
