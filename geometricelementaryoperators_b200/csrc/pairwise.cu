@@ -801,7 +801,7 @@ cudaError_t launch_f64_tma_dispatch(int neg, const CUtensorMap &ma, const CUtens
 // y = a b as Y' = A' rho(b) (geo::make_pair_tables: 1024 multiply-adds per
 // product instead of 4096) for Cl(6,0), Cl(5,1), Cl(2,4) and Cl(1,5), whose
 // tables are compile-time data (pair_tables_gen.h, written by
-// gen_pair_tables.cpp from the same host code): blade offsets are immediates
+// gen/gen_pair_tables.cpp from the same host code): blade offsets are immediates
 // and signs are negations inside the multiply-adds. A product is handled by four
 // lanes of a warp, lane l one kept row: it forms its 16 coefficients Ah[m] of a
 // from broadcast reads of the raw row (the four lanes read the same words; the

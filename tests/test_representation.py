@@ -31,7 +31,7 @@ def test_pair_tables(tmp_path):
     """The tables of the float64 pairwise representation kernel: the kernel's arithmetic on the host
     (geo::pair_product_host) equals the direct product for every D = 16 signature and operand reversal
     (tests/c/pair_check.cpp), and the compile-time copy the kernel uses (csrc/pair_tables_gen.h) is what
-    csrc/gen_pair_tables.cpp writes from them."""
+    csrc/gen/gen_pair_tables.cpp writes from them."""
     srcs = [str(CSRC / "representation.cpp"), str(CSRC / "plan_host.cpp")]
     inc = ["-I", str(ROOT / "include"), "-I", str(CSRC), "-I", "/usr/local/cuda/include"]
     exe = tmp_path / "pair_check"
@@ -41,7 +41,7 @@ def test_pair_tables(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     assert out.returncode == 0 and "PAIR_CHECK: PASS cases=112" in out.stdout, out.stdout + out.stderr
     gen = tmp_path / "gen_pair_tables"
-    res = subprocess.run(["g++", "-std=c++17", "-O2", *inc, str(CSRC / "gen_pair_tables.cpp"), *srcs, "-o", str(gen)],
+    res = subprocess.run(["g++", "-std=c++17", "-O2", *inc, str(CSRC / "gen" / "gen_pair_tables.cpp"), *srcs, "-o", str(gen)],
                          capture_output=True, text=True)
     assert res.returncode == 0, res.stderr
     header = subprocess.run([str(gen)], capture_output=True, text=True, timeout=60)
